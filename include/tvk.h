@@ -1,0 +1,89 @@
+/*
+ * tvk.h -- C ABI of the B200 (sm_100a) attention hot path for tinyvllm.
+ *
+ * Every entry point takes raw device pointers that the caller owns, plain
+ * integer sizes, a dtype code and a CUDA stream (as void*, 0 = legacy default
+ * stream).  Nothing here allocates device memory except where stated; scratch
+ * space is passed in by the caller.  All launches are stream-ordered and
+ * asynchronous.  Return value: TVK_OK (0) or a negative TVK_ERR_* code; the
+ * message for the last failure on the calling thread is tvk_last_error().
+ *
+ * Reference interfaces replaced (paths inside jonirajala/tinyvllm):
+ *   tvk_paged_decode_attention  <- paged_decode_attention   tinyvllm/model/llama.py:97-144
+ *   tvk_flash_prefill_attention <- flash_prefill_attention  tinyvllm/model/llama.py:58-94
+ *                                  + Attention._write_kv_to_blocks llama.py:188-209 (fused)
+ *   tvk_write_kv_slots          <- KVCache.write_kv          tinyvllm/core/kv_cache.py:34-38
+ *                                  (decode append loop       tinyvllm/model/llama.py:381-386)
+ */
+#ifndef TVK_H_
+#define TVK_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype codes (the reference supports float32 and float16: model/weights.py:44) */
+#define TVK_DTYPE_F32 0
+#define TVK_DTYPE_F16 1
+#define TVK_DTYPE_BF16 2
+
+/* status codes */
+#define TVK_OK 0
+#define TVK_ERR_INVALID (-1)     /* bad pointer, shape or size                     */
+#define TVK_ERR_UNSUPPORTED (-2) /* valid call, but no kernel for this shape/dtype */
+#define TVK_ERR_CUDA (-3)        /* a CUDA runtime call or launch failed           */
+#define TVK_ERR_WORKSPACE (-4)   /* workspace missing or too small                 */
+
+/* ABI version of this header (bumped on any signature change). */
+int tvk_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* tvk_last_error(void);
+
+/*
+ * Bytes of scratch that tvk_paged_decode_attention needs for a batch whose
+ * block tables are `max_blocks` wide: a 256-byte header (a device status word)
+ * followed by the split-K partials (fp32 output rows plus max / sum pairs).
+ * Replaces nothing in the reference (tinygrad allocates its temporaries).
+ */
+size_t tvk_paged_decode_workspace_size(int batch, int n_heads, int n_kv_heads, int head_dim,
+                                       int block_size, int max_blocks, int max_context_len);
+
+/*
+ * Paged-decode attention, one query token per sequence.
+ * Replaces paged_decode_attention (tinyvllm/model/llama.py:97-144).
+ *
+ *   q            [batch, 1, n_heads, head_dim]               dtype
+ *   k_cache      [num_blocks, block_size, n_kv_heads, head_dim] dtype (one layer)
+ *   v_cache      same shape as k_cache
+ *   block_tables int32 [batch, max_blocks], padded with any valid id (the
+ *                reference pads with block 0)
+ *   context_lens int32 [batch]
+ *   out          [batch, 1, n_heads, head_dim]               dtype
+ *   max_context_len  < 0 means "None" (attend over max_blocks*block_size
+ *                positions masked by context_lens, llama.py:113-118)
+ *
+ * out[b,0,h,:] = softmax_t(q[b,h].K[b,t,h/g] / sqrt(head_dim)) . V[b,t,h/g]
+ * over t < min(context_lens[b], table width), with g = n_heads / n_kv_heads and
+ * K[b,t] = k_cache[block_tables[b, t / block_size], t % block_size].
+ * A sequence with context_lens[b] <= 0 gets zeros (the reference's output is
+ * then a uniform average over the padded positions; the engine never does this).
+ * Block ids outside [0, num_blocks) read as zeros.
+ * Softmax and accumulation are float32 for every storage dtype.
+ */
+int tvk_paged_decode_attention(const void* q, const void* k_cache, const void* v_cache,
+                               const int32_t* block_tables, const int32_t* context_lens,
+                               void* out,
+                               int batch, int n_heads, int n_kv_heads, int head_dim,
+                               int block_size, int num_blocks, int max_blocks,
+                               int max_context_len, int dtype,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TVK_H_ */

@@ -1,0 +1,87 @@
+"""The C-ABI library loads and exports every symbol include/*.h declares (CPU only).
+
+No compute call is made here: only version / workspace arithmetic and argument
+validation paths that return before any CUDA call.
+"""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _declared_symbols():
+    names = set()
+    for h in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names.update(re.findall(r"\b(tvk_[a-z0-9_]+)\s*\(", text))
+    return sorted(names)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from tinyvllm_b200 import build
+    build.build()
+    from tinyvllm_b200 import _lib
+    return _lib.lib()
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = _declared_symbols()
+    assert "tvk_paged_decode_attention" in names
+    handle = ctypes.CDLL(str(ROOT / "tinyvllm_b200" / "libtvk.so"))
+    missing = [n for n in names if not hasattr(handle, n)]
+    assert not missing, f"declared but not exported: {missing}"
+
+
+def test_python_binding_covers_header(lib):
+    from tinyvllm_b200 import _lib
+    assert set(_declared_symbols()) <= set(_lib.SIGNATURES), "ctypes prototypes missing for some exports"
+
+
+def test_abi_version(lib):
+    assert lib.tvk_abi_version() == 1
+
+
+def test_workspace_size_arithmetic(lib):
+    hdr = 256
+    # config 1: short tables -> a split size that gives >1 split per sequence
+    n = lib.tvk_paged_decode_workspace_size(4, 32, 4, 64, 16, 16, -1)
+    assert n > hdr and (n - hdr) % (4 * 32 * (64 + 2) * 4) == 0
+    # one split fits -> header only
+    assert lib.tvk_paged_decode_workspace_size(4096, 32, 8, 128, 16, 4, -1) == hdr
+    # max_context_len truncates the table
+    a = lib.tvk_paged_decode_workspace_size(256, 32, 8, 128, 16, 256, -1)
+    b = lib.tvk_paged_decode_workspace_size(256, 32, 8, 128, 16, 256, 1024)
+    assert b < a
+
+
+def test_invalid_arguments_are_rejected_before_any_launch(lib):
+    rc = lib.tvk_paged_decode_attention(None, None, None, None, None, None, 1, 32, 4, 64, 16, 8, 4, -1, 1,
+                                        None, 0, None)
+    assert rc == -1 and b"null pointer" in lib.tvk_last_error()
+    fake = ctypes.c_void_p(256)
+    args = [fake] * 6
+    rc = lib.tvk_paged_decode_attention(*args, 1, 30, 4, 64, 16, 8, 4, -1, 1, None, 0, None)
+    assert rc == -1 and b"multiple" in lib.tvk_last_error()
+    rc = lib.tvk_paged_decode_attention(*args, 1, 32, 4, 96, 16, 8, 4, -1, 1, None, 0, None)
+    assert rc == -2
+    rc = lib.tvk_paged_decode_attention(*args, 1, 32, 4, 64, 16, 8, 4, -1, 7, None, 0, None)
+    assert rc == -1
+    # a table wider than one split needs a workspace
+    rc = lib.tvk_paged_decode_attention(*args, 1, 32, 4, 64, 16, 8, 64, -1, 1, None, 0, None)
+    assert rc == -4 and b"workspace" in lib.tvk_last_error()
+    assert lib.tvk_paged_decode_attention(*args, 0, 32, 4, 64, 16, 8, 4, -1, 1, None, 0, None) == 0
+
+
+def test_cpu_tensors_are_refused():
+    import torch
+    from tinyvllm_b200.attention import paged_decode_attention
+    q = torch.zeros(1, 1, 4, 32)
+    kc = torch.zeros(2, 16, 4, 32)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        paged_decode_attention(q, kc, kc, torch.zeros(1, 2, dtype=torch.int32),
+                               torch.ones(1, dtype=torch.int32), 4, 4, 32, 16)

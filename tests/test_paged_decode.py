@@ -1,0 +1,213 @@
+"""Parity of the sm_100a paged-decode kernels with the CPU oracle (GPU).
+
+Tolerances (from the hot-path contract): fp32 1e-3 max-abs; fp16/bf16 2e-2
+max-abs and 1e-2 mean-relative, against the fp32 oracle run on the same
+rounded inputs.
+"""
+
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as oa
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+TOL = {torch.float32: (1e-3, None), torch.float16: (2e-2, 1e-2), torch.bfloat16: (2e-2, 1e-2)}
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _check(got, expect, dtype):
+    max_abs, mean_rel = TOL[dtype]
+    g = _np(got).astype(np.float64)
+    e = np.asarray(expect, dtype=np.float64)
+    assert np.isfinite(g).all()
+    err = np.abs(g - e)
+    assert err.max() <= max_abs, f"max-abs {err.max()} > {max_abs}"
+    if mean_rel is not None:
+        rel = err.mean() / max(np.abs(e).mean(), 1e-12)
+        assert rel <= mean_rel, f"mean-rel {rel} > {mean_rel}"
+
+
+def _oracle(case, max_context_len=None):
+    return oa.paged_decode_attention(_np(case.q), _np(case.k_cache), _np(case.v_cache),
+                                     case.block_tables.cpu().numpy(), case.context_lens.cpu().numpy(),
+                                     case.n_heads, case.n_kv_heads, case.head_dim, case.block_size,
+                                     max_context_len)
+
+
+def _run(case, **kw):
+    from tinyvllm_b200.attention import paged_decode_attention
+    out = paged_decode_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.context_lens,
+                                 case.n_heads, case.n_kv_heads, case.head_dim, case.block_size, **kw)
+    torch.cuda.synchronize()
+    return out
+
+
+def test_config1_fp32_vs_oracle(cuda):
+    from tinyvllm_b200 import workloads
+    case = workloads.decode_config1(cuda)
+    _check(_run(case), _oracle(case), torch.float32)
+
+
+def test_golden_decode_config1(cuda):
+    g = np.load(GOLDEN / "decode_config1.npz")
+    hq, hkv, d, bs = (int(x) for x in g["meta"])
+    from tinyvllm_b200.attention import paged_decode_attention
+    for dtype in (torch.float32, torch.float16):
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+        out = paged_decode_attention(t(g["q"]).to(dtype), t(g["k_cache"]).to(dtype), t(g["v_cache"]).to(dtype),
+                                     t(g["block_tables"]), t(g["context_lens"]), hq, hkv, d, bs)
+        torch.cuda.synchronize()
+        _check(out, g["out"], dtype)
+
+
+# The reference tests' shapes (tests/test_paged_attention.py:126-251), contiguous tables.
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("batch,nh,nkv,d,ctx", [
+    (2, 8, 8, 64, 32), (1, 4, 4, 32, 32), (1, 32, 8, 64, 32), (1, 32, 4, 64, 64), (4, 8, 8, 32, 32),
+    (1, 4, 4, 32, 16), (1, 4, 4, 32, 64), (1, 4, 4, 32, 128), (1, 4, 4, 32, 25),
+])
+def test_reference_shapes(cuda, dtype, batch, nh, nkv, d, ctx):
+    from tinyvllm_b200 import workloads
+    case = workloads.decode_case(batch, nh, nkv, d, 16, [ctx] * batch, dtype=dtype, device=cuda,
+                                 seed=ctx * 7 + nh, contiguous=True)
+    _check(_run(case), _oracle(case), dtype)
+
+
+# Shuffled tables, ragged contexts, every supported head_dim / GQA group / block size.
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("d", [32, 64, 128])
+@pytest.mark.parametrize("nh,nkv", [(8, 8), (16, 8), (32, 8), (32, 4), (32, 2)])
+def test_shuffled_ragged(cuda, dtype, d, nh, nkv):
+    from tinyvllm_b200 import workloads
+    ctx = [1, 15, 16, 17, 63, 64, 65, 300, 1000]
+    case = workloads.decode_case(len(ctx), nh, nkv, d, 16, ctx, dtype=dtype, device=cuda, seed=nh + d)
+    _check(_run(case), _oracle(case), dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("bs", [1, 5, 8, 16, 32, 64])
+def test_block_sizes(cuda, dtype, bs):
+    from tinyvllm_b200 import workloads
+    ctx = [1, bs, bs + 1, 3 * bs + 2, 200]
+    case = workloads.decode_case(len(ctx), 32, 4, 64, bs, ctx, dtype=dtype, device=cuda, seed=bs)
+    _check(_run(case), _oracle(case), dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+def test_engine_padding_width_64(cuda, dtype):
+    """The engine pads every table to 64 blocks with block 0 (engine.py:81,235-255)."""
+    from tinyvllm_b200 import workloads
+    ctx = [5, 100, 700, 1024]
+    case = workloads.decode_case(len(ctx), 32, 4, 64, 16, ctx, dtype=dtype, device=cuda, seed=11, width=64)
+    _check(_run(case), _oracle(case), dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+def test_context_beyond_table_is_truncated(cuda, dtype):
+    """ctx larger than table width: the reference attends only over the table (llama.py:117-118)."""
+    from tinyvllm_b200 import workloads
+    case = workloads.decode_case(3, 32, 8, 128, 16, [40, 64, 64], dtype=dtype, device=cuda, seed=12)
+    case.context_lens = torch.tensor([40, 5000, 64], dtype=torch.int32, device=cuda)
+    _check(_run(case), _oracle(case), dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+@pytest.mark.parametrize("mcl", [1, 16, 100, 1000])
+def test_max_context_len(cuda, dtype, mcl):
+    from tinyvllm_b200 import workloads
+    ctx = [10, 90, 400, 700]
+    case = workloads.decode_case(len(ctx), 32, 4, 64, 16, ctx, dtype=dtype, device=cuda, seed=mcl)
+    _check(_run(case, max_context_len=mcl), _oracle(case, mcl), dtype)
+
+
+def test_zero_context_gives_zeros(cuda):
+    """Documented deviation: ctx <= 0 -> zeros (the reference would average padding)."""
+    from tinyvllm_b200 import workloads
+    case = workloads.decode_case(3, 32, 4, 64, 16, [0, 20, 0], dtype=torch.float16, device=cuda, seed=13)
+    out = _run(case)
+    assert torch.count_nonzero(out[0]) == 0 and torch.count_nonzero(out[2]) == 0
+    ref = _oracle(case)
+    _check(out[1:2], ref[1:2], torch.float16)
+
+
+def test_out_of_range_block_ids_read_zero(cuda):
+    from tinyvllm_b200 import workloads
+    for dtype in (torch.float16, torch.float32):
+        case = workloads.decode_case(1, 32, 4, 64, 16, [48], dtype=dtype, device=cuda, seed=14)
+        n = case.k_cache.shape[0]
+        case.block_tables[0, 1] = n + 100   # second block points outside the pool
+        out = _run(case)
+        kc, vc = case.k_cache.clone(), case.v_cache.clone()
+        kc = torch.cat([kc, torch.zeros_like(kc[:1])])
+        vc = torch.cat([vc, torch.zeros_like(vc[:1])])
+        bt = case.block_tables.clone()
+        bt[0, 1] = n   # the appended zero block
+        ref = oa.paged_decode_attention(_np(case.q), _np(kc), _np(vc), bt.cpu().numpy(),
+                                        case.context_lens.cpu().numpy(), 32, 4, 64, 16)
+        _check(out, ref, dtype)
+
+
+def test_nan_outside_context_does_not_leak(cuda):
+    """Stale non-finite values past the context (same block) must not reach the output."""
+    from tinyvllm_b200 import workloads
+    for dtype in (torch.float16, torch.bfloat16, torch.float32):
+        case = workloads.decode_case(2, 32, 8, 128, 16, [20, 33], dtype=dtype, device=cuda, seed=15)
+        ref = _oracle(case)
+        for b, c in enumerate([20, 33]):
+            blk = int(case.block_tables[b, c // 16])
+            case.k_cache[blk, c % 16:] = float("nan")
+            case.v_cache[blk, c % 16:] = float("inf")
+        _check(_run(case), ref, dtype)
+
+
+def test_config3_subset_vs_oracle(cuda):
+    """Full config-3 batch on the GPU; 12 sequences checked against the oracle."""
+    from tinyvllm_b200 import workloads
+    case = workloads.decode_config3(cuda)
+    out = _run(case)
+    assert torch.isfinite(out.float()).all()
+    idx = [0, 1, 2, 50, 99, 128, 170, 200, 230, 253, 254, 255]
+    bt = case.block_tables[idx]
+    used = torch.unique(bt)
+    remap = torch.full((case.k_cache.shape[0],), -1, dtype=torch.int64, device=cuda)
+    remap[used.long()] = torch.arange(len(used), device=cuda)
+    sub_bt = remap[bt.long()].int()
+    ref = oa.paged_decode_attention(_np(case.q[idx]), _np(case.k_cache[used.long()]), _np(case.v_cache[used.long()]),
+                                    sub_bt.cpu().numpy(), case.context_lens[idx].cpu().numpy(), 32, 8, 128, 16)
+    _check(out[idx], ref, torch.float16)
+
+
+def test_config3_relabel_invariance(cuda):
+    """Size-independent property at full size: permuting physical block ids (and the
+    tables with them) leaves the output bit-identical."""
+    from tinyvllm_b200 import workloads
+    case = workloads.decode_config3(cuda)
+    out = _run(case).clone()
+    n = case.k_cache.shape[0]
+    g = torch.Generator(device=cuda).manual_seed(99)
+    perm = torch.randperm(n, device=cuda, generator=g)          # new id of old block i
+    kc = torch.empty_like(case.k_cache)
+    vc = torch.empty_like(case.v_cache)
+    kc[perm] = case.k_cache
+    vc[perm] = case.v_cache
+    case.k_cache, case.v_cache = kc, vc
+    case.block_tables = perm[case.block_tables.long()].int()
+    out2 = _run(case)
+    assert torch.equal(out, out2)
+
+
+def test_repeat_calls_are_deterministic(cuda):
+    from tinyvllm_b200 import workloads
+    case = workloads.decode_config3(cuda, batch=64)
+    a = _run(case).clone()
+    b = _run(case)
+    assert torch.equal(a, b)

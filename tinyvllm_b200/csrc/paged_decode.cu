@@ -1,0 +1,706 @@
+// paged_decode.cu -- paged-decode attention for sm_100a.
+//
+// Replaces paged_decode_attention (tinyvllm/model/llama.py:97-144).  The
+// reference gathers every table entry into a dense [B, maxctx, Hkv, D] copy,
+// materialises the GQA expand and runs two batched matmuls over the padded
+// length.  Here each CTA owns one (sequence, KV head, context split) and reads
+// only the blocks that hold live tokens, once, for all n_heads/n_kv_heads query
+// heads that share that KV head.
+//
+// Two kernels:
+//  * tc  (fp16 / bf16, block_size in {8,16,32,64}, head_dim in {32,64,128}):
+//    one producer warp issues 4-D TMA loads of whole K/V blocks (one KV head,
+//    all block_size rows, swizzled) into a multi-stage shared-memory ring
+//    guarded by mbarriers; four consumer warps each take 16 tokens of a stage
+//    and run Q.K^T and P.V on the tensor cores (m16n8k16, fp32 accumulate) with
+//    the GQA group as the M dimension, and an fp32 online softmax in registers.
+//  * simt (any dtype incl. fp32, any block size): cooperative vector loads of
+//    32-token tiles into shared memory and fp32 CUDA-core math.
+// Sequences longer than one split are reduced by a small combine kernel from
+// fp32 partials (max, sum, unnormalised output) kept in the caller workspace.
+#include <math.h>
+
+#include "tvk_common.cuh"
+
+namespace {
+
+constexpr int kStageTok = 64;  // tokens per pipeline stage / split granularity
+constexpr int kSimtTile = 32;  // tokens per tile in the simt kernel
+constexpr int kMaxGroup = 16;  // query heads per KV head (MMA M dimension)
+
+struct DecodeParams {
+  const void* q;
+  void* out;
+  const int32_t* block_tables;
+  const int32_t* context_lens;
+  const void* k_cache;  // simt path only
+  const void* v_cache;  // simt path only
+  float* part_o;        // [B, Hq, max_splits, D]
+  float* part_ml;       // [B, Hq, max_splits, 2]
+  int* status;          // may be null
+  int batch, n_heads, n_kv_heads, group, head_dim, block_size, num_blocks, max_blocks;
+  int max_ctx_tokens;  // (possibly truncated) table width * block_size
+  int split_tokens;    // tokens per CTA, multiple of kStageTok
+  int max_splits;
+  float scale_log2;  // log2(e) / sqrt(head_dim)
+};
+
+__device__ __forceinline__ void report_timeout(int* status) {
+  if (status) atomicExch(status, tvk::kStatusWaitTimeout);
+}
+
+// Effective context of sequence b (the reference never looks past the table).
+__device__ __forceinline__ int effective_ctx(const DecodeParams& p, int b) {
+  int c = p.context_lens[b];
+  return c < p.max_ctx_tokens ? c : p.max_ctx_tokens;
+}
+
+// Byte offset of 16-byte chunk k16 of row t inside a TMA-swizzled tile whose
+// rows are RB bytes (128 -> SWIZZLE_128B, 64 -> SWIZZLE_64B).
+template <int RB>
+__device__ __forceinline__ uint32_t swz(int t, int k16) {
+  if constexpr (RB == 128) {
+    return t * 128 + ((k16 ^ (t & 7)) << 4);
+  } else {
+    return t * 64 + ((k16 ^ ((t >> 1) & 3)) << 4);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void write_zero_rows(const DecodeParams& p, int b, int kvh) {
+  T* out = reinterpret_cast<T*>(p.out);
+  const int n = p.group * p.head_dim;
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    out[((size_t)b * p.n_heads + kvh * p.group) * p.head_dim + i] = DT<T>::from_f(0.f);
+}
+
+// -----------------------------------------------------------------------------
+// Tensor-core kernel (fp16 / bf16)
+// -----------------------------------------------------------------------------
+template <int D, int RB>
+struct TcCfg {
+  static constexpr int kChunks = D * 2 / RB;               // row chunks per token
+  static constexpr int kChunkBytes = kStageTok * RB;       // one chunk of one stage
+  static constexpr int kKVBytes = kChunks * kChunkBytes;   // K (or V) part of a stage
+  static constexpr int kStageBytes = 2 * kKVBytes;
+  static constexpr int kStages = D == 128 ? 3 : (D == 64 ? 5 : 8);
+  static constexpr int kRingBytes = kStages * kStageBytes;
+  static constexpr int kCombineBytes = 4 * kMaxGroup * (D + 2) * 4;
+  static constexpr int kBodyBytes = kRingBytes > kCombineBytes ? kRingBytes : kCombineBytes;
+  static constexpr int kBarOffset = kBodyBytes;
+  static constexpr int kSmemBytes = kBarOffset + 2 * kStages * 8 + 1024;  // +1024 alignment slack
+};
+
+template <typename T, int D, int RB>
+__global__ void __launch_bounds__(160, 2)
+    paged_decode_tc_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm_k,
+                           const __grid_constant__ CUtensorMap tm_v) {
+  using C = TcCfg<D, RB>;
+  constexpr int RC = RB / 2;  // elements per row chunk
+  constexpr int K16_PER_ROW = RB / 16;
+
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int ctx = effective_ctx(p, b);
+  if (ctx <= 0) {
+    if (split == 0) write_zero_rows<T>(p, b, kvh);
+    return;
+  }
+  const int tok_begin = split * p.split_tokens;
+  if (tok_begin >= ctx) return;
+  const int n_tok = min(p.split_tokens, ctx - tok_begin);
+  const int n_iters = (n_tok + kStageTok - 1) / kStageTok;
+  const int nsplit = (ctx + p.split_tokens - 1) / p.split_tokens;
+  const int bs = p.block_size;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = ptx::smem_u32(smem_raw);
+  const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
+  uint8_t* base = smem_raw + (base_u32 - raw_u32);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(base + C::kBarOffset);
+  uint64_t* empty_bar = full_bar + C::kStages;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      ptx::mbar_init(&full_bar[s], 1);
+      ptx::mbar_init(&empty_bar[s], 4);
+    }
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 4) {
+    // ---------------- producer warp: TMA loads of whole K/V blocks ----------
+    if (lane == 0) {
+      ptx::prefetch_tmap(&tm_k);
+      ptx::prefetch_tmap(&tm_v);
+    }
+    const int32_t* bt = p.block_tables + (size_t)b * p.max_blocks;
+    for (int it = 0; it < n_iters; ++it) {
+      const int s = it % C::kStages;
+      const uint32_t ph = (it / C::kStages) & 1;
+      if (!ptx::mbar_wait(&empty_bar[s], ph ^ 1)) {
+        report_timeout(p.status);
+        return;
+      }
+      const int tok0 = tok_begin + it * kStageTok;  // absolute token of stage row 0
+      const int live = min(kStageTok, ctx - tok0);
+      const int nblk = (live + bs - 1) / bs;
+      if (lane == 0) ptx::mbar_arrive_expect_tx(&full_bar[s], (uint32_t)(nblk * bs * D * 2 * 2));
+      __syncwarp();
+      const uint32_t stage_off = s * C::kStageBytes;
+      const int n_loads = nblk * C::kChunks * 2;
+      for (int i = lane; i < n_loads; i += 32) {
+        const int j = i / (C::kChunks * 2);
+        const int rest = i % (C::kChunks * 2);
+        const int kv = rest / C::kChunks;
+        const int c = rest % C::kChunks;
+        const int blk = __ldg(bt + tok0 / bs + j);
+        uint8_t* dst = base + stage_off + kv * C::kKVBytes + c * C::kChunkBytes + j * bs * RB;
+        ptx::tma_load_4d(dst, kv ? &tm_v : &tm_k, &full_bar[s], c * RC, kvh, 0, blk);
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumer warps ----------------------------------------
+  const int g = lane >> 2, tig = lane & 3;
+  const int G = p.group;
+
+  // Q fragments (A operand, rows = query heads of this KV group, zero padded).
+  uint32_t qa[D / 16][4];
+  {
+    const T* q = reinterpret_cast<const T*>(p.q) + ((size_t)b * p.n_heads + kvh * G) * D;
+    const uint32_t* q32 = reinterpret_cast<const uint32_t*>(q);
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      const int c0 = kk * 16 + tig * 2;
+      qa[kk][0] = g < G ? q32[(g * D + c0) >> 1] : 0u;
+      qa[kk][1] = g + 8 < G ? q32[((g + 8) * D + c0) >> 1] : 0u;
+      qa[kk][2] = g < G ? q32[(g * D + c0 + 8) >> 1] : 0u;
+      qa[kk][3] = g + 8 < G ? q32[((g + 8) * D + c0 + 8) >> 1] : 0u;
+    }
+  }
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+
+  bool ok = true;
+  for (int it = 0; it < n_iters; ++it) {
+    const int s = it % C::kStages;
+    const uint32_t ph = (it / C::kStages) & 1;
+    if (!ptx::mbar_wait(&full_bar[s], ph)) {
+      ok = false;
+      break;
+    }
+    const int t_base = it * kStageTok + warp * 16;  // token of this warp's row 0, relative to split
+    if (t_base < n_tok) {
+      const uint32_t kbase = base_u32 + s * C::kStageBytes;
+      const uint32_t vbase = kbase + C::kKVBytes;
+      const int row0 = warp * 16;
+
+      // S = Q K^T  (16 heads x 16 tokens)
+      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const int chunk16 = kk * 2 + ((lane >> 3) & 1);
+        const int c = chunk16 / K16_PER_ROW, k16 = chunk16 % K16_PER_ROW;
+        const int t = row0 + (lane & 7) + ((lane >> 4) << 3);
+        uint32_t r0, r1, r2, r3;
+        ptx::ldmatrix_x4(kbase + c * C::kChunkBytes + swz<RB>(t, k16), r0, r1, r2, r3);
+        ptx::Mma<T>::run(sc[0], qa[kk], r0, r1);
+        ptx::Mma<T>::run(sc[1], qa[kk], r2, r3);
+      }
+
+      // scale, mask, online softmax (fp32, log2 domain)
+      const bool partial = t_base + 16 > n_tok;
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int tok = t_base + n * 8 + tig * 2 + (j & 1);
+          sc[n][j] = (!partial || tok < n_tok) ? sc[n][j] * p.scale_log2 : -INFINITY;
+        }
+      float mx0 = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+      float mx1 = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float corr0 = exp2f(m0 - mn0), corr1 = exp2f(m1 - mn1);
+      m0 = mn0;
+      m1 = mn1;
+      float pr[2][4];
+#pragma unroll
+      for (int n = 0; n < 2; ++n) {
+        pr[n][0] = exp2f(sc[n][0] - mn0);
+        pr[n][1] = exp2f(sc[n][1] - mn0);
+        pr[n][2] = exp2f(sc[n][2] - mn1);
+        pr[n][3] = exp2f(sc[n][3] - mn1);
+      }
+      l0 = l0 * corr0 + (pr[0][0] + pr[0][1] + pr[1][0] + pr[1][1]);
+      l1 = l1 * corr1 + (pr[0][2] + pr[0][3] + pr[1][2] + pr[1][3]);
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) {
+        o[i][0] *= corr0;
+        o[i][1] *= corr0;
+        o[i][2] *= corr1;
+        o[i][3] *= corr1;
+      }
+      uint32_t pa[4];
+      pa[0] = DT<T>::pack2(pr[0][0], pr[0][1]);
+      pa[1] = DT<T>::pack2(pr[0][2], pr[0][3]);
+      pa[2] = DT<T>::pack2(pr[1][0], pr[1][1]);
+      pa[3] = DT<T>::pack2(pr[1][2], pr[1][3]);
+
+      // Rows past the context may hold stale shared memory: zero their V.
+      uint32_t vm_lo = 0xffffffffu, vm_hi = 0xffffffffu;
+      if (partial) {
+        const int tl = t_base + tig * 2, th = t_base + 8 + tig * 2;
+        vm_lo = (tl < n_tok ? 0x0000ffffu : 0u) | (tl + 1 < n_tok ? 0xffff0000u : 0u);
+        vm_hi = (th < n_tok ? 0x0000ffffu : 0u) | (th + 1 < n_tok ? 0xffff0000u : 0u);
+      }
+
+      // O += P V
+#pragma unroll
+      for (int np = 0; np < D / 16; ++np) {
+        const int chunk16 = np * 2 + (lane >> 4);
+        const int c = chunk16 / K16_PER_ROW, k16 = chunk16 % K16_PER_ROW;
+        const int t = row0 + (lane & 7) + (((lane >> 3) & 1) << 3);
+        uint32_t r0, r1, r2, r3;
+        ptx::ldmatrix_x4_trans(vbase + c * C::kChunkBytes + swz<RB>(t, k16), r0, r1, r2, r3);
+        r0 &= vm_lo;
+        r1 &= vm_hi;
+        r2 &= vm_lo;
+        r3 &= vm_hi;
+        ptx::Mma<T>::run(o[2 * np], pa, r0, r1);
+        ptx::Mma<T>::run(o[2 * np + 1], pa, r2, r3);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(&empty_bar[s]);
+  }
+  if (!ok) {
+    report_timeout(p.status);
+    return;
+  }
+
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+
+  // ---------------- combine the four warps through shared memory ----------
+  ptx::named_barrier_sync(1, 128);  // every consumer is done reading the ring
+  float* cm = reinterpret_cast<float*>(base);
+  float* cl = cm + 4 * kMaxGroup;
+  float* co = cl + 4 * kMaxGroup;
+  if (tig == 0) {
+    cm[warp * 16 + g] = m0;
+    cm[warp * 16 + g + 8] = m1;
+    cl[warp * 16 + g] = l0;
+    cl[warp * 16 + g + 8] = l1;
+  }
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) {
+    const int col = i * 8 + tig * 2;
+    co[(warp * 16 + g) * D + col] = o[i][0];
+    co[(warp * 16 + g) * D + col + 1] = o[i][1];
+    co[(warp * 16 + g + 8) * D + col] = o[i][2];
+    co[(warp * 16 + g + 8) * D + col + 1] = o[i][3];
+  }
+  ptx::named_barrier_sync(1, 128);
+
+  for (int idx = threadIdx.x; idx < G * D; idx += 128) {
+    const int r = idx / D, col = idx % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, cm[w * 16 + r]);
+    float L = 0.f, A = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float e = exp2f(cm[w * 16 + r] - M);
+      L += cl[w * 16 + r] * e;
+      A += co[(w * 16 + r) * D + col] * e;
+    }
+    const int h = kvh * G + r;
+    if (nsplit == 1) {
+      reinterpret_cast<T*>(p.out)[((size_t)b * p.n_heads + h) * D + col] = DT<T>::from_f(A / L);
+    } else {
+      const size_t row = ((size_t)b * p.n_heads + h) * p.max_splits + split;
+      p.part_o[row * D + col] = A;
+      if (col == 0) {
+        p.part_ml[row * 2] = M;
+        p.part_ml[row * 2 + 1] = L;
+      }
+    }
+  }
+}
+
+// -----------------------------------------------------------------------------
+// SIMT kernel (any dtype, any block size)
+// -----------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ void load4(const T* src, float* dst) {
+  if constexpr (sizeof(T) == 4) {
+    const float4 v = *reinterpret_cast<const float4*>(src);
+    dst[0] = v.x;
+    dst[1] = v.y;
+    dst[2] = v.z;
+    dst[3] = v.w;
+  } else {
+    const uint2 v = *reinterpret_cast<const uint2*>(src);
+    const T* h = reinterpret_cast<const T*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[i] = DT<T>::to_f(h[i]);
+  }
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(128) paged_decode_simt_kernel(const DecodeParams p) {
+  constexpr int DP = D + 4;               // padded row (floats)
+  constexpr int MAXK = kMaxGroup * D / 128;  // (head, dim) outputs per thread
+  __shared__ __align__(16) float qs[kMaxGroup][D];
+  __shared__ __align__(16) float ks[kSimtTile][DP];
+  __shared__ __align__(16) float vs[kSimtTile][DP];
+  __shared__ float ps[kMaxGroup][kSimtTile];
+  __shared__ float corr_s[kMaxGroup];
+  __shared__ float mfin[kMaxGroup], lfin[kMaxGroup];
+
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int ctx = effective_ctx(p, b);
+  if (ctx <= 0) {
+    if (split == 0) write_zero_rows<T>(p, b, kvh);
+    return;
+  }
+  const int tok_begin = split * p.split_tokens;
+  if (tok_begin >= ctx) return;
+  const int n_tok = min(p.split_tokens, ctx - tok_begin);
+  const int nsplit = (ctx + p.split_tokens - 1) / p.split_tokens;
+  const int G = p.group, Hkv = p.n_kv_heads, bs = p.block_size;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  const T* q = reinterpret_cast<const T*>(p.q) + ((size_t)b * p.n_heads + kvh * G) * D;
+  for (int i = tid; i < G * D; i += 128) qs[i / D][i % D] = DT<T>::to_f(q[i]);
+
+  const T* kc = reinterpret_cast<const T*>(p.k_cache);
+  const T* vc = reinterpret_cast<const T*>(p.v_cache);
+  const int32_t* bt = p.block_tables + (size_t)b * p.max_blocks;
+
+  float acc[MAXK];
+#pragma unroll
+  for (int k = 0; k < MAXK; ++k) acc[k] = 0.f;
+  // online-softmax state of heads owned by this warp (g = warp + 4*i)
+  float m_own[kMaxGroup / 4], l_own[kMaxGroup / 4];
+#pragma unroll
+  for (int i = 0; i < kMaxGroup / 4; ++i) {
+    m_own[i] = -INFINITY;
+    l_own[i] = 0.f;
+  }
+
+  for (int t0 = 0; t0 < n_tok; t0 += kSimtTile) {
+    __syncthreads();
+    for (int i = tid; i < kSimtTile * (D / 4); i += 128) {
+      const int t = i / (D / 4), d4 = (i % (D / 4)) * 4;
+      float kv4[4] = {0.f, 0.f, 0.f, 0.f}, vv4[4] = {0.f, 0.f, 0.f, 0.f};
+      const int tok = t0 + t;
+      if (tok < n_tok) {
+        const int abs_tok = tok_begin + tok;
+        const int blk = __ldg(bt + abs_tok / bs);
+        if (blk >= 0 && blk < p.num_blocks) {
+          const size_t off = (((size_t)blk * bs + abs_tok % bs) * Hkv + kvh) * D + d4;
+          load4<T>(kc + off, kv4);
+          load4<T>(vc + off, vv4);
+        }
+      }
+      *reinterpret_cast<float4*>(&ks[t][d4]) = make_float4(kv4[0], kv4[1], kv4[2], kv4[3]);
+      *reinterpret_cast<float4*>(&vs[t][d4]) = make_float4(vv4[0], vv4[1], vv4[2], vv4[3]);
+    }
+    __syncthreads();
+
+    // scores: warp owns heads warp, warp+4, ...; lane = token
+#pragma unroll
+    for (int i = 0; i < kMaxGroup / 4; ++i) {
+      const int gh = warp + 4 * i;
+      if (gh < G) {
+        float s = 0.f;
+#pragma unroll 8
+        for (int d = 0; d < D; d += 4) {
+          const float4 kk = *reinterpret_cast<const float4*>(&ks[lane][d]);
+          const float4 qq = *reinterpret_cast<const float4*>(&qs[gh][d]);
+          s = fmaf(qq.x, kk.x, s);
+          s = fmaf(qq.y, kk.y, s);
+          s = fmaf(qq.z, kk.z, s);
+          s = fmaf(qq.w, kk.w, s);
+        }
+        s = (t0 + lane < n_tok) ? s * p.scale_log2 : -INFINITY;
+        float mx = s;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float mn = fmaxf(m_own[i], mx);
+        const float corr = exp2f(m_own[i] - mn);
+        const float pv = exp2f(s - mn);
+        float sum = pv;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        l_own[i] = l_own[i] * corr + sum;
+        m_own[i] = mn;
+        ps[gh][lane] = pv;
+        if (lane == 0) corr_s[gh] = corr;
+      }
+    }
+    __syncthreads();
+
+#pragma unroll
+    for (int k = 0; k < MAXK; ++k) {
+      const int idx = tid + 128 * k;
+      if (idx < G * D) {
+        const int gh = idx / D, d = idx % D;
+        float a = acc[k] * corr_s[gh];
+#pragma unroll 8
+        for (int t = 0; t < kSimtTile; ++t) a = fmaf(ps[gh][t], vs[t][d], a);
+        acc[k] = a;
+      }
+    }
+  }
+
+#pragma unroll
+  for (int i = 0; i < kMaxGroup / 4; ++i) {
+    const int gh = warp + 4 * i;
+    if (gh < G && lane == 0) {
+      mfin[gh] = m_own[i];
+      lfin[gh] = l_own[i];
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < MAXK; ++k) {
+    const int idx = tid + 128 * k;
+    if (idx < G * D) {
+      const int gh = idx / D, d = idx % D;
+      const int h = kvh * G + gh;
+      if (nsplit == 1) {
+        reinterpret_cast<T*>(p.out)[((size_t)b * p.n_heads + h) * D + d] = DT<T>::from_f(acc[k] / lfin[gh]);
+      } else {
+        const size_t row = ((size_t)b * p.n_heads + h) * p.max_splits + split;
+        p.part_o[row * D + d] = acc[k];
+        if (d == 0) {
+          p.part_ml[row * 2] = mfin[gh];
+          p.part_ml[row * 2 + 1] = lfin[gh];
+        }
+      }
+    }
+  }
+}
+
+// -----------------------------------------------------------------------------
+// split-K combine
+// -----------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(128) paged_decode_combine_kernel(const DecodeParams p) {
+  const int kvh = blockIdx.x, b = blockIdx.y;
+  const int ctx = effective_ctx(p, b);
+  if (ctx <= 0) return;
+  const int nsplit = (ctx + p.split_tokens - 1) / p.split_tokens;
+  if (nsplit <= 1) return;
+  const int G = p.group, D = p.head_dim;
+  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+    const int r = idx / D, col = idx % D;
+    const int h = kvh * G + r;
+    const size_t row0 = ((size_t)b * p.n_heads + h) * p.max_splits;
+    float M = -INFINITY;
+    for (int i = 0; i < nsplit; ++i) M = fmaxf(M, p.part_ml[(row0 + i) * 2]);
+    float L = 0.f, A = 0.f;
+    for (int i = 0; i < nsplit; ++i) {
+      const float e = exp2f(p.part_ml[(row0 + i) * 2] - M);
+      L += p.part_ml[(row0 + i) * 2 + 1] * e;
+      A += p.part_o[(row0 + i) * D + col] * e;
+    }
+    reinterpret_cast<T*>(p.out)[((size_t)b * p.n_heads + h) * D + col] = DT<T>::from_f(A / L);
+  }
+}
+
+// -----------------------------------------------------------------------------
+// host side
+// -----------------------------------------------------------------------------
+constexpr int kTargetCtas = 148 * 8;
+
+int table_tokens(int block_size, int max_blocks, int max_context_len) {
+  int blocks = max_blocks;
+  if (max_context_len >= 0) {
+    const int need = (max_context_len + block_size - 1) / block_size;
+    blocks = need < max_blocks ? need : max_blocks;
+  }
+  return blocks * block_size;
+}
+
+// Tokens per CTA: the largest of 512/256/128/64 that still gives enough CTAs
+// to fill the GPU when every sequence uses its whole table.
+int choose_split(int batch, int n_kv_heads, int max_ctx_tokens) {
+  const long units = (long)batch * n_kv_heads;
+  for (int s = 512; s > kStageTok; s >>= 1)
+    if (units * ((max_ctx_tokens + s - 1) / s) >= kTargetCtas) return s;
+  return kStageTok;
+}
+
+size_t workspace_bytes_for(int batch, int n_heads, int head_dim, int max_splits) {
+  size_t bytes = tvk::kWorkspaceHeader;
+  if (max_splits > 1) bytes += (size_t)batch * n_heads * max_splits * (head_dim + 2) * sizeof(float);
+  return bytes;
+}
+
+template <typename T, int D, int RB>
+int launch_tc(const DecodeParams& p, const void* k_cache, const void* v_cache, CUtensorMapDataType tdt,
+              cudaStream_t stream) {
+  using C = TcCfg<D, RB>;
+  tvk::EncodeTiledFn encode = tvk::encode_tiled_fn();
+  if (!encode) {
+    tvk::set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return TVK_ERR_CUDA;
+  }
+  const size_t es = sizeof(T);
+  CUtensorMap tmk, tmv;
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)p.n_kv_heads, (cuuint64_t)p.block_size,
+                        (cuuint64_t)p.num_blocks};
+  cuuint64_t strides[3] = {(cuuint64_t)(D * es), (cuuint64_t)(p.n_kv_heads * D * es),
+                           (cuuint64_t)((size_t)p.block_size * p.n_kv_heads * D * es)};
+  cuuint32_t box[4] = {(cuuint32_t)(RB / es), 1u, (cuuint32_t)p.block_size, 1u};
+  cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  const CUtensorMapSwizzle sw = RB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUresult r1 = encode(&tmk, tdt, 4, const_cast<void*>(k_cache), dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r2 = encode(&tmv, tdt, 4, const_cast<void*>(v_cache), dims, strides, box, estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r1 != CUDA_SUCCESS || r2 != CUDA_SUCCESS) {
+    tvk::set_error("cuTensorMapEncodeTiled failed (%d, %d)", (int)r1, (int)r2);
+    return TVK_ERR_CUDA;
+  }
+  auto kern = paged_decode_tc_kernel<T, D, RB>;
+  static unsigned long long attr_set_mask = 0;  // per instantiation, one bit per device
+  int dev = 0;
+  TVK_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev >= 64 || !(attr_set_mask & (1ull << dev))) {
+    TVK_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
+    if (dev < 64) attr_set_mask |= (1ull << dev);
+  }
+  dim3 grid(p.max_splits, p.n_kv_heads, p.batch);
+  kern<<<grid, 160, C::kSmemBytes, stream>>>(p, tmk, tmv);
+  TVK_CHECK_LAUNCH("paged_decode_tc");
+  return TVK_OK;
+}
+
+template <typename T>
+int launch_typed(DecodeParams& p, bool use_tc, CUtensorMapDataType tdt, cudaStream_t stream) {
+  int rc = TVK_OK;
+  if (use_tc) {
+    if constexpr (sizeof(T) == 2) {
+      switch (p.head_dim) {
+        case 32: rc = launch_tc<T, 32, 64>(p, p.k_cache, p.v_cache, tdt, stream); break;
+        case 64: rc = launch_tc<T, 64, 128>(p, p.k_cache, p.v_cache, tdt, stream); break;
+        default: rc = launch_tc<T, 128, 128>(p, p.k_cache, p.v_cache, tdt, stream); break;
+      }
+    }
+  } else {
+    dim3 grid(p.max_splits, p.n_kv_heads, p.batch);
+    switch (p.head_dim) {
+      case 32: paged_decode_simt_kernel<T, 32><<<grid, 128, 0, stream>>>(p); break;
+      case 64: paged_decode_simt_kernel<T, 64><<<grid, 128, 0, stream>>>(p); break;
+      default: paged_decode_simt_kernel<T, 128><<<grid, 128, 0, stream>>>(p); break;
+    }
+    TVK_CHECK_LAUNCH("paged_decode_simt");
+  }
+  if (rc != TVK_OK) return rc;
+  if (p.max_splits > 1) {
+    paged_decode_combine_kernel<T><<<dim3(p.n_kv_heads, p.batch), 128, 0, stream>>>(p);
+    TVK_CHECK_LAUNCH("paged_decode_combine");
+  }
+  return TVK_OK;
+}
+
+}  // namespace
+
+extern "C" size_t tvk_paged_decode_workspace_size(int batch, int n_heads, int n_kv_heads, int head_dim,
+                                                  int block_size, int max_blocks, int max_context_len) {
+  if (batch <= 0 || n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 || max_blocks <= 0)
+    return tvk::kWorkspaceHeader;
+  const int tt = table_tokens(block_size, max_blocks, max_context_len);
+  const int split = choose_split(batch, n_kv_heads, tt);
+  const int max_splits = (tt + split - 1) / split;
+  return workspace_bytes_for(batch, n_heads, head_dim, max_splits);
+}
+
+extern "C" int tvk_paged_decode_attention(const void* q, const void* k_cache, const void* v_cache,
+                                          const int32_t* block_tables, const int32_t* context_lens, void* out,
+                                          int batch, int n_heads, int n_kv_heads, int head_dim, int block_size,
+                                          int num_blocks, int max_blocks, int max_context_len, int dtype,
+                                          void* workspace, size_t workspace_bytes, void* stream) {
+  TVK_CHECK_ARG(batch >= 0, "batch must be >= 0 (got %d)", batch);
+  if (batch == 0) return TVK_OK;
+  TVK_CHECK_ARG(q && k_cache && v_cache && block_tables && context_lens && out, "null pointer argument");
+  TVK_CHECK_ARG(n_heads > 0 && n_kv_heads > 0 && n_heads % n_kv_heads == 0,
+                "n_heads (%d) must be a positive multiple of n_kv_heads (%d)", n_heads, n_kv_heads);
+  TVK_CHECK_ARG(n_heads / n_kv_heads <= kMaxGroup, "n_heads / n_kv_heads = %d exceeds %d", n_heads / n_kv_heads,
+                kMaxGroup);
+  TVK_CHECK_ARG(batch <= 65535 && n_kv_heads <= 65535, "batch and n_kv_heads must be <= 65535");
+  TVK_CHECK_ARG(block_size > 0 && num_blocks > 0 && max_blocks > 0,
+                "block_size, num_blocks and max_blocks must be positive");
+  TVK_CHECK_ARG(dtype == TVK_DTYPE_F32 || dtype == TVK_DTYPE_F16 || dtype == TVK_DTYPE_BF16, "unknown dtype %d",
+                dtype);
+  if (head_dim != 32 && head_dim != 64 && head_dim != 128) {
+    tvk::set_error("head_dim %d unsupported (32, 64 or 128)", head_dim);
+    return TVK_ERR_UNSUPPORTED;
+  }
+  const size_t es = tvk::dtype_size(dtype);
+  TVK_CHECK_ARG(((uintptr_t)q % 16 == 0) && ((uintptr_t)k_cache % 16 == 0) && ((uintptr_t)v_cache % 16 == 0) &&
+                    ((uintptr_t)out % 4 == 0),
+                "q, k_cache and v_cache must be 16-byte aligned");
+
+  DecodeParams p{};
+  p.q = q;
+  p.out = out;
+  p.block_tables = block_tables;
+  p.context_lens = context_lens;
+  p.k_cache = k_cache;
+  p.v_cache = v_cache;
+  p.batch = batch;
+  p.n_heads = n_heads;
+  p.n_kv_heads = n_kv_heads;
+  p.group = n_heads / n_kv_heads;
+  p.head_dim = head_dim;
+  p.block_size = block_size;
+  p.num_blocks = num_blocks;
+  p.max_blocks = max_blocks;
+  p.max_ctx_tokens = table_tokens(block_size, max_blocks, max_context_len);
+  p.split_tokens = choose_split(batch, n_kv_heads, p.max_ctx_tokens);
+  p.max_splits = p.max_ctx_tokens > 0 ? (p.max_ctx_tokens + p.split_tokens - 1) / p.split_tokens : 1;
+  p.scale_log2 = (float)(1.4426950408889634 / sqrt((double)head_dim));
+
+  const size_t need = workspace_bytes_for(batch, n_heads, head_dim, p.max_splits);
+  if (p.max_splits > 1) {
+    if (!workspace || workspace_bytes < need) {
+      tvk::set_error("workspace of %zu bytes needed, %zu given", need, workspace ? workspace_bytes : (size_t)0);
+      return TVK_ERR_WORKSPACE;
+    }
+  }
+  if (workspace) {
+    TVK_CHECK_ARG((uintptr_t)workspace % 16 == 0, "workspace must be 16-byte aligned");
+    p.status = reinterpret_cast<int*>(workspace);
+    float* f = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + tvk::kWorkspaceHeader);
+    p.part_o = f;
+    p.part_ml = f + (size_t)batch * n_heads * p.max_splits * head_dim;
+  }
+
+  const bool tc_shape = (block_size == 8 || block_size == 16 || block_size == 32 || block_size == 64);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  (void)es;
+  switch (dtype) {
+    case TVK_DTYPE_F16: return launch_typed<__half>(p, tc_shape, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, s);
+    case TVK_DTYPE_BF16: return launch_typed<__nv_bfloat16>(p, tc_shape, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, s);
+    default: return launch_typed<float>(p, false, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, s);
+  }
+}
