@@ -83,6 +83,35 @@ int tvk_paged_decode_attention(const void* q, const void* k_cache, const void* v
                                void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Paged-decode attention that allocates nothing (no counterpart in the
+ * reference, which lets tinygrad allocate its temporaries).
+ *
+ * Same arguments and result as tvk_paged_decode_attention, minus the
+ * workspace: the split-K scratch is a fixed 64 MiB array compiled into this
+ * library (TVK_NOALLOC_SCRATCH_BYTES), held by every GPU that loads the
+ * library until the process exits.  It is for callers that cannot allocate
+ * device memory: an engine that gives (nearly) all free HBM to its KV pool at
+ * start-up, a host binding without a device allocator of its own, or a decode
+ * loop that cannot take cudaMalloc's device-wide synchronisation.
+ *
+ * A call whose scratch need (tvk_paged_decode_workspace_size) exceeds the
+ * array returns TVK_ERR_WORKSPACE without launching anything.  No cudaMalloc,
+ * cudaFree or other allocating routine is called.  The first call on each
+ * device looks the array's device address up (cudaGetSymbolAddress, with that
+ * device current); make that first call before any stream capture.  Every
+ * call shares the one array and the array keeps the last call's contents:
+ * calls whose kernels overlap on the GPU (different streams, or different
+ * threads) race on it and must be serialised by the caller.
+ */
+#define TVK_NOALLOC_SCRATCH_BYTES (64ull << 20)
+int tvk_paged_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                       const int32_t* block_tables, const int32_t* context_lens,
+                                       void* out,
+                                       int batch, int n_heads, int n_kv_heads, int head_dim,
+                                       int block_size, int num_blocks, int max_blocks,
+                                       int max_context_len, int dtype, void* stream);
+
+/*
  * Tensor-core layout self-test (no reference counterpart): one 128 x n x k
  * tcgen05 GEMM through the operand paths the prefill kernel uses (thread-
  * written swizzled A, TMA-loaded B, TMEM accumulator).

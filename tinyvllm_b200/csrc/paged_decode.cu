@@ -20,6 +20,8 @@
 // fp32 partials (max, sum, unnormalised output) kept in the caller workspace.
 #include <math.h>
 
+#include <mutex>
+
 #include "tvk_common.cuh"
 
 namespace {
@@ -703,4 +705,78 @@ extern "C" int tvk_paged_decode_attention(const void* q, const void* k_cache, co
     case TVK_DTYPE_BF16: return launch_typed<__nv_bfloat16>(p, tc_shape, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, s);
     default: return launch_typed<float>(p, false, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, s);
   }
+}
+
+// -----------------------------------------------------------------------------
+// Paged decode without any device allocation.
+//
+// For callers that cannot allocate device memory for the split-K scratch: an
+// engine that hands (nearly) all free HBM to its KV pool at start-up, as
+// tinyvllm sizes its pool from free GPU memory, leaving no room for per-call
+// buffers; a host binding (ctypes, cgo, JNI) that has no device allocator of
+// its own; or a decode loop that cannot afford cudaMalloc's implicit device
+// synchronisation.  This entry point uses a fixed scratch array compiled into
+// the library instead of a caller workspace.
+// -----------------------------------------------------------------------------
+namespace {
+
+// Every GPU that loads this library holds this array until the process exits.
+// 64 MiB covers the split-K partials of 256 sequences x 32 heads x 4096-token
+// tables at head_dim 128 (34 MB); larger calls are refused.
+constexpr size_t kNoAllocScratchBytes = 64ull << 20;
+__device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_dev_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on the current device.  The host-side
+// symbol `g_noalloc_scratch` is only a stand-in: passing it to a kernel would
+// fault (or silently touch host memory), so the real address is looked up once
+// per device with that device current.
+int noalloc_scratch_ptr(void** out) {
+  int dev = 0;
+  TVK_CHECK_CUDA(cudaGetDevice(&dev));
+  TVK_CHECK_ARG(dev >= 0 && dev < kNoAllocMaxDevices, "device %d beyond the %d supported", dev, kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_dev_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      tvk::set_error("cudaGetSymbolAddress(g_noalloc_scratch) failed on device %d: %s", dev, cudaGetErrorString(e));
+      return TVK_ERR_CUDA;
+    }
+    g_noalloc_dev_ptr[dev] = p;
+  }
+  *out = g_noalloc_dev_ptr[dev];
+  return TVK_OK;
+}
+
+}  // namespace
+
+extern "C" int tvk_paged_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                                  const int32_t* block_tables, const int32_t* context_lens,
+                                                  void* out, int batch, int n_heads, int n_kv_heads, int head_dim,
+                                                  int block_size, int num_blocks, int max_blocks,
+                                                  int max_context_len, int dtype, void* stream) {
+  TVK_CHECK_ARG(batch >= 0, "batch must be >= 0 (got %d)", batch);
+  if (batch == 0) return TVK_OK;
+  const size_t need = tvk_paged_decode_workspace_size(batch, n_heads, n_kv_heads, head_dim, block_size, max_blocks,
+                                                      max_context_len);
+  if (need > kNoAllocScratchBytes) {
+    tvk::set_error(
+        "this call needs %zu bytes of split-K scratch; the no-allocation entry point has a fixed %zu bytes "
+        "(use tvk_paged_decode_attention with a caller workspace)",
+        need, kNoAllocScratchBytes);
+    return TVK_ERR_WORKSPACE;
+  }
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch_ptr(&scratch);
+  if (rc != TVK_OK) return rc;
+  // The scratch keeps the previous call's contents; only the status word has
+  // to start at zero (the split-K partials are written before they are read).
+  TVK_CHECK_CUDA(cudaMemsetAsync(scratch, 0, sizeof(int), reinterpret_cast<cudaStream_t>(stream)));
+  return tvk_paged_decode_attention(q, k_cache, v_cache, block_tables, context_lens, out, batch, n_heads, n_kv_heads,
+                                    head_dim, block_size, num_blocks, max_blocks, max_context_len, dtype, scratch,
+                                    kNoAllocScratchBytes, stream);
 }
