@@ -83,6 +83,35 @@ int tvk_paged_decode_attention(const void* q, const void* k_cache, const void* v
                                void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Causal (or full) prefill attention over a ragged batch of prompts, with the
+ * prompt K/V written into the paged pool by the same kernel.
+ * Replaces flash_prefill_attention (tinyvllm/model/llama.py:58-94) and the
+ * block-chunked writes of Attention._write_kv_to_blocks (llama.py:188-209,
+ * core/kv_cache.py:34-38).  The reference handles one prompt per call
+ * (inputs [1, L, H, D]); n_seqs == 1 is that case.
+ *
+ *   q    [total_tokens, n_heads, head_dim]      prompts packed along tokens
+ *   k, v [total_tokens, n_kv_heads, head_dim]   (post-RoPE k, as the reference writes)
+ *   out  [total_tokens, n_heads, head_dim]
+ *   cu_seqlens int32 [n_seqs + 1] on the device: prompt s is tokens
+ *              [cu_seqlens[s], cu_seqlens[s+1]); max_seqlen >= every length
+ *   causal     key j is visible to query i iff j <= i (else all keys of the prompt)
+ *   slot_mapping int64 [total_tokens] or NULL: when given, token t's k/v rows are
+ *              also stored at k_cache/v_cache [num_blocks, block_size, n_kv_heads,
+ *              head_dim] flat slot slot_mapping[t] (= block * block_size + offset);
+ *              negative or out-of-pool slots are skipped.
+ *   workspace  optional (>= 4 bytes): its first int is set to 1 if a bounded wait expired.
+ * fp16/bf16 with head_dim 64 or 128 run on tcgen05 (TMEM accumulators, TMA
+ * loads); fp32 and head_dim 32 use a CUDA-core kernel.  Softmax is fp32.
+ */
+int tvk_flash_prefill_attention(const void* q, const void* k, const void* v, void* out,
+                                const int32_t* cu_seqlens, int n_seqs, int max_seqlen, int total_tokens,
+                                int n_heads, int n_kv_heads, int head_dim, int causal, int dtype,
+                                const int64_t* slot_mapping, void* k_cache, void* v_cache,
+                                int num_blocks, int block_size,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Paged-decode attention that allocates nothing (no counterpart in the
  * reference, which lets tinygrad allocate its temporaries).
  *

@@ -1,0 +1,193 @@
+"""Parity of the flash-prefill kernels (tcgen05 and SIMT) with the CPU oracle, and
+the fused paged K/V write against the reference slot mapping (GPU).
+
+Tolerances: fp32 1e-3 max-abs (the reference tests use 1e-4..1e-3 between two
+fp32 paths); fp16/bf16 2e-2 max-abs and 1e-2 mean-relative.  The paged write
+is checked bit-exactly.
+"""
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as oa
+from oracle import paging as op
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+TOL = {torch.float32: (1e-3, None), torch.float16: (2e-2, 1e-2), torch.bfloat16: (2e-2, 1e-2)}
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _check(got, expect, dtype):
+    max_abs, mean_rel = TOL[dtype]
+    g = _np(got).astype(np.float64)
+    e = np.asarray(expect, dtype=np.float64)
+    assert np.isfinite(g).all()
+    err = np.abs(g - e)
+    assert err.max() <= max_abs, f"max-abs {err.max()} > {max_abs}"
+    if mean_rel is not None:
+        rel = err.mean() / max(np.abs(e).mean(), 1e-12)
+        assert rel <= mean_rel, f"mean-rel {rel} > {mean_rel}"
+
+
+def _rand(shape, dtype, g, dev):
+    return torch.randn(shape, generator=g, device=dev).to(dtype)
+
+
+def _flash(q, k, v, causal=True):
+    from tinyvllm_b200.attention import flash_prefill_attention
+    out = flash_prefill_attention(q[None], k[None], v[None], causal)[0]
+    torch.cuda.synchronize()
+    return out
+
+
+def _oracle(q, k, v, causal=True):
+    return oa.flash_prefill_attention(_np(q)[None], _np(k)[None], _np(v)[None], causal)[0]
+
+
+DTYPES = [torch.float32, torch.float16, torch.bfloat16]
+
+
+# tests/test_flash_attention.py shapes
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("L", [1, 2, 7, 8, 15, 16, 31, 32, 63, 64, 128])
+@pytest.mark.parametrize("D", [32, 64, 128])
+def test_lengths_and_head_dims(cuda, dtype, L, D):
+    g = torch.Generator(device=cuda).manual_seed(L * 10 + D)
+    q, k, v = (_rand((L, 4, D), dtype, g, cuda) for _ in range(3))
+    _check(_flash(q, k, v), _oracle(q, k, v), dtype)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("L,nh,nkv,D", [(16, 8, 4, 32), (16, 32, 8, 64), (16, 32, 4, 64), (32, 32, 8, 64),
+                                        (64, 32, 8, 64), (256, 32, 8, 64), (200, 32, 4, 128), (1, 8, 8, 64)])
+def test_gqa(cuda, dtype, L, nh, nkv, D):
+    g = torch.Generator(device=cuda).manual_seed(L + nh + nkv + D)
+    q = _rand((L, nh, D), dtype, g, cuda)
+    k = _rand((L, nkv, D), dtype, g, cuda)
+    v = _rand((L, nkv, D), dtype, g, cuda)
+    _check(_flash(q, k, v), _oracle(q, k, v), dtype)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("L,D", [(16, 32), (16, 64), (300, 64), (129, 128)])
+def test_non_causal(cuda, dtype, L, D):
+    g = torch.Generator(device=cuda).manual_seed(L + D)
+    q, k, v = (_rand((L, 4, D), dtype, g, cuda) for _ in range(3))
+    _check(_flash(q, k, v, causal=False), _oracle(q, k, v, causal=False), dtype)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_first_token_attends_to_itself(cuda, dtype):
+    """tests/test_flash_attention.py:123-130 (head_dim 16 there; 32 here, the smallest kernel size)."""
+    q = torch.zeros(8, 2, 32, device=cuda)
+    q[0] = 1.0
+    k = torch.randn(8, 2, 32, generator=torch.Generator(device=cuda).manual_seed(1), device=cuda)
+    v = torch.zeros(8, 2, 32, device=cuda)
+    v[:, :, :8] = torch.eye(8, device=cuda)[:, None, :]
+    out = _flash(q.to(dtype), k.to(dtype), v.to(dtype))
+    assert out[0, 0, 0].item() > 0.5
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("D", [32, 64, 128])
+def test_last_token_mean(cuda, dtype, D):
+    """tests/test_flash_attention.py:132-139: last row of v = arange(8) averages to 3.5."""
+    q = torch.ones(8, 2, D, device=cuda, dtype=dtype)
+    k = torch.zeros(8, 2, D, device=cuda, dtype=dtype)
+    v = torch.arange(8, device=cuda, dtype=torch.float32).reshape(8, 1, 1).expand(8, 2, D).contiguous().to(dtype)
+    assert abs(_flash(q, k, v)[-1, 0, 0].item() - 3.5) < 1e-2
+
+
+def _config2_inputs(dev, dtype=torch.float16, lens=(1, 15, 16, 17, 128, 500, 1024, 2048), D=64, nkv=4):
+    g = torch.Generator(device=dev).manual_seed(1236)
+    T = sum(lens)
+    q = _rand((T, 32, D), dtype, g, dev)
+    k = _rand((T, nkv, D), dtype, g, dev)
+    v = _rand((T, nkv, D), dtype, g, dev)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=dev)
+    return q, k, v, cu, list(lens)
+
+
+@pytest.mark.parametrize("dtype,D,nkv", [(torch.float16, 64, 4), (torch.bfloat16, 128, 8), (torch.float32, 64, 4)])
+def test_config2_ragged_batch_with_paged_write(cuda, dtype, D, nkv):
+    """Config 2: 8 ragged prompts in one call; attention vs oracle per prompt and the
+    paged pool bit-exact against the reference slot mapping (LIFO allocation)."""
+    from tinyvllm_b200.attention import flash_prefill_attention_varlen
+    q, k, v, cu, lens = _config2_inputs(cuda, dtype, D=D, nkv=nkv)
+    gold = np.load(GOLDEN / "prefill_slots_config2.npz")
+    assert list(gold["lens"]) == lens
+    slots = torch.from_numpy(gold["slot_mapping"]).to(cuda)
+    kc = torch.zeros(1024, 16, nkv, D, dtype=dtype, device=cuda)
+    vc = torch.zeros_like(kc)
+    out = flash_prefill_attention_varlen(q, k, v, cu, max(lens), True, slot_mapping=slots, k_cache=kc, v_cache=vc)
+    torch.cuda.synchronize()
+    # paged write: every token's row at its slot, everything else untouched (zero)
+    exp_k = torch.zeros(1024 * 16, nkv, D, dtype=dtype, device=cuda)
+    exp_v = torch.zeros_like(exp_k)
+    exp_k[slots] = k
+    exp_v[slots] = v
+    assert torch.equal(kc.view(-1, nkv, D), exp_k)
+    assert torch.equal(vc.view(-1, nkv, D), exp_v)
+    # attention, prompt by prompt
+    for i, L in enumerate(lens):
+        a, b = int(cu[i]), int(cu[i + 1])
+        _check(out[a:b], _oracle(q[a:b], k[a:b], v[a:b]), dtype)
+
+
+def test_paged_write_matches_chunked_reference_write(cuda):
+    """The fused write equals the reference's block-chunked write_kv sequence
+    (llama.py:188-209) replayed by the oracle on the same BlockManager state."""
+    from tinyvllm_b200.attention import flash_prefill_attention_varlen
+    lens = [5, 40, 16, 33]
+    q, k, v, cu, _ = _config2_inputs(cuda, torch.float16, lens=lens)
+    bm = op.OracleBlockManager(1, 32, 16)
+    cache = op.OracleKVCache(1, 32, 16, 4, 64, dtype=np.float16)
+    slots = []
+    kn, vn = k.cpu().numpy(), v.cpu().numpy()
+    for sid, L in enumerate(lens):
+        bm.register_sequence(sid)
+        a, b = int(cu[sid]), int(cu[sid + 1])
+        op.write_prompt_kv(cache, bm, 0, sid, kn[a:b], vn[a:b], 0)
+        t = bm.get_block_table(sid)
+        slots += [t[p // 16] * 16 + p % 16 for p in range(L)]
+    kc = torch.zeros(32, 16, 4, 64, dtype=torch.float16, device=cuda)
+    vc = torch.zeros_like(kc)
+    flash_prefill_attention_varlen(q, k, v, cu, max(lens), True,
+                                   slot_mapping=torch.tensor(slots, dtype=torch.int64, device=cuda),
+                                   k_cache=kc, v_cache=vc)
+    torch.cuda.synchronize()
+    assert np.array_equal(kc.cpu().numpy(), cache.k_cache[0])
+    assert np.array_equal(vc.cpu().numpy(), cache.v_cache[0])
+
+
+def test_negative_slots_are_skipped(cuda):
+    from tinyvllm_b200.attention import flash_prefill_attention_varlen
+    q, k, v, cu, lens = _config2_inputs(cuda, torch.float16, lens=[20])
+    slots = torch.arange(20, dtype=torch.int64, device=cuda)
+    slots[3] = -1
+    slots[7] = 10 ** 9  # beyond the pool
+    kc = torch.zeros(4, 16, 4, 64, dtype=torch.float16, device=cuda)
+    vc = torch.zeros_like(kc)
+    flash_prefill_attention_varlen(q, k, v, cu, 20, True, slot_mapping=slots, k_cache=kc, v_cache=vc)
+    torch.cuda.synchronize()
+    flat = kc.view(-1, 4, 64)
+    keep = [i for i in range(20) if i not in (3, 7)]
+    assert torch.equal(flat[keep], k[keep])
+    assert torch.count_nonzero(flat[3]) == 0 and torch.count_nonzero(flat[7]) == 0
+
+
+def test_repeat_calls_are_deterministic(cuda):
+    from tinyvllm_b200.attention import flash_prefill_attention_varlen
+    q, k, v, cu, lens = _config2_inputs(cuda, torch.float16)
+    a = flash_prefill_attention_varlen(q, k, v, cu, max(lens)).clone()
+    b = flash_prefill_attention_varlen(q, k, v, cu, max(lens))
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)

@@ -84,3 +84,73 @@ def paged_decode_attention(queries: torch.Tensor, k_cache: torch.Tensor, v_cache
         _lib.dtype_code(k_cache), ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
     _lib.check(rc, "tvk_paged_decode_attention")
     return out
+
+
+def flash_prefill_attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                                   cu_seqlens: torch.Tensor, max_seqlen: int, causal: bool = True, *,
+                                   slot_mapping: Optional[torch.Tensor] = None,
+                                   k_cache: Optional[torch.Tensor] = None,
+                                   v_cache: Optional[torch.Tensor] = None,
+                                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Causal (or full) attention over a ragged batch of prompts packed along tokens.
+
+    q [T,Hq,D], k/v [T,Hkv,D]; ``cu_seqlens`` int32 [n+1] prefix sums of the prompt
+    lengths (device); ``max_seqlen`` >= the longest prompt.  With ``slot_mapping``
+    (int64 [T], device; -1 skips a token) the kernel also writes each token's k/v
+    row into ``k_cache/v_cache`` [N,block_size,Hkv,D] at flat slot
+    ``block*block_size + offset`` -- the paged write of llama.py:188-209 fused
+    into the attention kernel.  Returns [T,Hq,D].
+    """
+    tensors = [q, k, v, cu_seqlens] + [t for t in (slot_mapping, k_cache, v_cache) if t is not None]
+    dev = _lib.require_cuda(*tensors)
+    if q.dim() != 3 or k.dim() != 3 or v.shape != k.shape or q.shape[0] != k.shape[0] or q.shape[2] != k.shape[2]:
+        raise ValueError(f"q must be [T,Hq,D] and k/v [T,Hkv,D]; got {tuple(q.shape)}, {tuple(k.shape)}, "
+                         f"{tuple(v.shape)}")
+    if q.dtype != k.dtype or v.dtype != k.dtype:
+        raise TypeError("q, k and v must share one dtype")
+    if cu_seqlens.dtype != torch.int32 or cu_seqlens.dim() != 1:
+        raise TypeError("cu_seqlens must be a 1-D int32 tensor")
+    for name, t in (("q", q), ("k", k), ("v", v), ("cu_seqlens", cu_seqlens)):
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    T, Hq, D = q.shape
+    Hkv = k.shape[1]
+    n_seqs = cu_seqlens.shape[0] - 1
+    num_blocks = block_size = 0
+    if slot_mapping is not None:
+        if k_cache is None or v_cache is None:
+            raise ValueError("slot_mapping needs k_cache and v_cache")
+        if slot_mapping.dtype != torch.int64 or slot_mapping.shape != (T,):
+            raise TypeError("slot_mapping must be int64 [T]")
+        if (k_cache.dim() != 4 or k_cache.shape[2:] != (Hkv, D) or v_cache.shape != k_cache.shape
+                or k_cache.dtype != q.dtype or v_cache.dtype != q.dtype
+                or not k_cache.is_contiguous() or not v_cache.is_contiguous()):
+            raise ValueError("k_cache/v_cache must be contiguous [N,block_size,Hkv,D] in the dtype of q")
+        num_blocks, block_size = k_cache.shape[0], k_cache.shape[1]
+    if out is None:
+        out = torch.empty_like(q)
+    ws = _workspace(dev, 256)
+    L = _lib.lib()
+    rc = L.tvk_flash_prefill_attention(
+        _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(out), _lib.ptr(cu_seqlens), n_seqs, int(max_seqlen), T,
+        Hq, Hkv, D, 1 if causal else 0, _lib.dtype_code(q), _lib.ptr(slot_mapping), _lib.ptr(k_cache),
+        _lib.ptr(v_cache), num_blocks, block_size, ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+    _lib.check(rc, "tvk_flash_prefill_attention")
+    return out
+
+
+def flash_prefill_attention(queries: torch.Tensor, keys: torch.Tensor, values: torch.Tensor,
+                            causal: bool = True) -> torch.Tensor:
+    """Flash attention for prefill (tinyvllm/model/llama.py:58-94).
+
+    Inputs [1,L,H,D] (keys/values may have fewer heads, GQA); returns [1,L,Hq,D].
+    """
+    dev = _lib.require_cuda(queries, keys, values)
+    if queries.dim() != 4 or queries.shape[0] != 1:
+        raise ValueError("queries must be [1,L,H,D]")
+    q = queries[0].contiguous()
+    k = keys[0].contiguous()
+    v = values[0].contiguous()
+    L = q.shape[0]
+    cu = torch.tensor([0, L], dtype=torch.int32, device=dev)
+    return flash_prefill_attention_varlen(q, k, v, cu, L, causal)[None]

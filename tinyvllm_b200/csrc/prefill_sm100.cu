@@ -1,0 +1,597 @@
+// prefill_sm100.cu -- causal flash prefill with the fused paged K/V write.
+//
+// Replaces flash_prefill_attention (tinyvllm/model/llama.py:58-94) and the
+// per-block K/V writes of Attention._write_kv_to_blocks (llama.py:188-209,
+// core/kv_cache.py:34-38).  The reference materialises the whole [H, L, L]
+// score matrix, expands GQA heads and masks after the full Q.K^T; here each CTA
+// owns one 128-row query tile of one head of one prompt, walks only the key
+// tiles at or below the diagonal, and never leaves the chip with scores.
+//
+// tcgen05 kernel (fp16/bf16, head_dim 64 or 128), 6 warps:
+//   warp 0  TMA producer: Q once, then K/V 128-token tiles into a ring; for the
+//           diagonal tile (this CTA's own tokens) of the first query head of a
+//           KV group it also copies the landed K/V rows into their paged slots.
+//   warp 1  owns TMEM (512 columns) and issues the MMAs from one thread:
+//           S_j = Q.K_j^T (M=128, N=128, fp32 in TMEM, double buffered) and
+//           O_j = P_j.V_j (M=128, N=head_dim, fp32 in TMEM, double buffered).
+//   warps 2-5  softmax: one query row per thread, S read with tcgen05.ld,
+//           online softmax in the log2 domain, P written to shared memory in
+//           the 128-byte swizzled K-major layout, O_j folded into a register
+//           accumulator with the running rescale.
+// SIMT kernel (any dtype incl. fp32, head_dim 32/64/128): one warp per four
+// query rows, fp32 CUDA-core math; also does the paged write.
+#include <math.h>
+
+#include <type_traits>
+
+#include "tvk_common.cuh"
+#include "sm100_umma.cuh"
+
+namespace {
+
+struct PrefillParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  const int32_t* cu_seqlens;
+  const int64_t* slot_mapping;  // may be null: no paged write
+  void* k_cache;
+  void* v_cache;
+  int* status;  // may be null
+  int n_seqs, n_heads, n_kv_heads, group, head_dim, causal, num_blocks, block_size, n_mtiles;
+  float scale_log2;
+};
+
+__device__ __forceinline__ void report(int* status) {
+  if (status) atomicExch(status, tvk::kStatusWaitTimeout);
+}
+
+// Bounded mbarrier wait shared by all roles of a CTA: gives up after 2 s, or at
+// once when another thread of the CTA already gave up (abort flag in smem).
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                              uint64_t limit_ns = 2000000000ull) {
+  if (ptx::mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = ptx::globaltimer();
+  while (true) {
+    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (ptx::globaltimer() - t0 > limit_ns) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* m, uint64_t* bar, int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(ptx::smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(c2), "r"(ptx::smem_u32(bar))
+      : "memory");
+}
+
+template <int D>
+struct PfCfg {
+  static constexpr int kKB = D / 64;                 // 64-element (128 B) column blocks per row
+  static constexpr int kBlockBytes = 128 * 128;      // one column block of a 128-row tile
+  static constexpr int kTileBytes = 128 * D * 2;     // one 128-row tile of Q, K or V
+  static constexpr int kStages = D == 64 ? 3 : 2;
+  static constexpr int kQOff = 0;
+  static constexpr int kKOff = kQOff + kTileBytes;
+  static constexpr int kVOff = kKOff + kStages * kTileBytes;
+  static constexpr int kPOff = kVOff + kStages * kTileBytes;
+  static constexpr int kPBytes = 128 * 128 * 2;      // P tile: 128 rows x 128 tokens
+  static constexpr int kBarOff = kPOff + 2 * kPBytes;
+  // q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], s_empty[2], p_full[2], o_full[2], o_empty[2], final
+  static constexpr int kNumBars = 1 + 3 * kStages + 10 + 1;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag
+  static constexpr int kSmemBytes = kMiscOff + 16 + 1024;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kOCol = 256;  // O buffers at columns 256 and 256 + D; S at 0 and 128
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(192, 1)
+    flash_prefill_tc_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tm_q,
+                            const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
+  using C = PfCfg<D>;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  const int seq = blockIdx.z, h = blockIdx.y;
+  const int mtile = p.n_mtiles - 1 - (int)blockIdx.x;  // heaviest tiles first
+  const int s0 = p.cu_seqlens[seq];
+  const int L = p.cu_seqlens[seq + 1] - s0;
+  if (mtile * 128 >= L) return;
+  const int kvh = h / p.group;
+  const int n_kv = p.causal ? mtile + 1 : (L + 127) / 128;
+  const bool write_kv = p.slot_mapping != nullptr && (h % p.group) == 0;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = ptx::smem_u32(smem_raw);
+  const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
+  uint8_t* base = smem_raw + (base_u32 - raw_u32);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + C::kBarOff);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = q_full + 1;
+  uint64_t* v_full = k_full + C::kStages;
+  uint64_t* kv_empty = v_full + C::kStages;
+  uint64_t* s_full = kv_empty + C::kStages;
+  uint64_t* s_empty = s_full + 2;
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* o_full = p_full + 2;
+  uint64_t* o_empty = o_full + 2;
+  uint64_t* final_bar = o_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + C::kMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(base + C::kMiscOff + 4);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 1) {
+    umma::tmem_alloc(tmem_slot, C::kTmemCols);
+    umma::tmem_relinquish();
+  }
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(q_full, 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      ptx::mbar_init(&k_full[s], 1);
+      ptx::mbar_init(&v_full[s], 1);
+      ptx::mbar_init(&kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(&s_full[b], 1);
+      ptx::mbar_init(&s_empty[b], 4);
+      ptx::mbar_init(&p_full[b], 4);
+      ptx::mbar_init(&o_full[b], 1);
+      ptx::mbar_init(&o_empty[b], 4);
+    }
+    ptx::mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // =========================== TMA producer ===============================
+    int issued = 0;
+    bool ok = true;
+    if (lane == 0) {
+      ptx::prefetch_tmap(&tm_q);
+      ptx::prefetch_tmap(&tm_k);
+      ptx::prefetch_tmap(&tm_v);
+      ptx::mbar_arrive_expect_tx(q_full, C::kTileBytes);
+      for (int kb = 0; kb < C::kKB; ++kb)
+        tma_load_3d(base + C::kQOff + kb * C::kBlockBytes, &tm_q, q_full, kb * 64, h, s0 + mtile * 128);
+    }
+    for (int j = 0; j < n_kv; ++j) {
+      const int st = j % C::kStages;
+      const uint32_t ph = (j / C::kStages) & 1;
+      ok = wait_or_abort(&kv_empty[st], ph ^ 1, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      uint8_t* ks = base + C::kKOff + st * C::kTileBytes;
+      uint8_t* vs = base + C::kVOff + st * C::kTileBytes;
+      if (lane == 0) {
+        ptx::mbar_arrive_expect_tx(&k_full[st], C::kTileBytes);
+        for (int kb = 0; kb < C::kKB; ++kb)
+          tma_load_3d(ks + kb * C::kBlockBytes, &tm_k, &k_full[st], kb * 64, kvh, s0 + j * 128);
+        ptx::mbar_arrive_expect_tx(&v_full[st], C::kTileBytes);
+        for (int kb = 0; kb < C::kKB; ++kb)
+          tma_load_3d(vs + kb * C::kBlockBytes, &tm_v, &v_full[st], kb * 64, kvh, s0 + j * 128);
+      }
+      issued = j + 1;
+      if (write_kv && j == mtile) {
+        // The diagonal tile holds exactly this query tile's own tokens: copy the
+        // landed rows into their paged slots (slot = block * block_size + offset).
+        ok = wait_or_abort(&k_full[st], ph, abort_flag) && wait_or_abort(&v_full[st], ph, abort_flag);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        const int rows = min(128, L - mtile * 128);
+        const long long n_slots = (long long)p.num_blocks * p.block_size;
+        T* kc = reinterpret_cast<T*>(p.k_cache);
+        T* vc = reinterpret_cast<T*>(p.v_cache);
+        for (int i = lane; i < rows * (D / 8); i += 32) {
+          const int r = i / (D / 8), c8 = i % (D / 8);
+          const long long slot = p.slot_mapping[s0 + mtile * 128 + r];
+          if (slot < 0 || slot >= n_slots) continue;
+          const uint32_t off = (c8 / 8) * C::kBlockBytes + r * 128 + ((((c8 & 7) ^ (r & 7))) << 4);
+          const size_t dst = ((size_t)slot * p.n_kv_heads + kvh) * D + c8 * 8;
+          *reinterpret_cast<uint4*>(kc + dst) = *reinterpret_cast<const uint4*>(ks + off);
+          *reinterpret_cast<uint4*>(vc + dst) = *reinterpret_cast<const uint4*>(vs + off);
+        }
+      }
+    }
+    if (!ok) report(p.status);
+    // Do not leave with copies in flight: the last issued stages must have landed.
+    if (lane == 0) {
+      for (int j = issued - C::kStages < 0 ? 0 : issued - C::kStages; j < issued; ++j) {
+        const int st = j % C::kStages;
+        const uint32_t ph = (j / C::kStages) & 1;
+        ptx::mbar_wait(&k_full[st], ph, 100000000ull);
+        ptx::mbar_wait(&v_full[st], ph, 100000000ull);
+      }
+      ptx::mbar_wait(q_full, 0, 100000000ull);
+    }
+  } else if (warp == 1) {
+    // =========================== MMA issuer =================================
+    if (lane == 0) {
+      const uint32_t idesc_s = umma::idesc_f16(128, 128, kBf16, false);
+      const uint32_t idesc_o = umma::idesc_f16(128, D, kBf16, true);
+      const uint32_t q_addr = base_u32 + C::kQOff;
+      bool ok = wait_or_abort(q_full, 0, abort_flag);
+      auto issue_pv = [&](int i) -> bool {
+        const int st = i % C::kStages;
+        const uint32_t ph = (i / C::kStages) & 1;
+        const int b = i & 1;
+        const uint32_t pb = (i >> 1) & 1;
+        if (!wait_or_abort(&p_full[b], pb, abort_flag)) return false;
+        if (!wait_or_abort(&o_empty[b], pb ^ 1, abort_flag)) return false;
+        if (!wait_or_abort(&v_full[st], ph, abort_flag)) return false;
+        umma::fence_after_sync();
+        const uint32_t p_addr = base_u32 + C::kPOff + b * C::kPBytes;
+        const uint32_t v_addr = base_u32 + C::kVOff + st * C::kTileBytes;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint64_t ad = umma::smem_desc_sw128(p_addr + (ks >> 2) * C::kBlockBytes + (ks & 3) * 32, 16, 1024);
+          const uint64_t bd = umma::smem_desc_sw128(v_addr + ks * 2048, C::kBlockBytes, 1024);
+          umma::mma_f16_ss(tmem + C::kOCol + b * D, ad, bd, idesc_o, ks > 0 ? 1u : 0u);
+        }
+        umma::commit(&o_full[b]);
+        umma::commit(&kv_empty[st]);
+        return true;
+      };
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j % C::kStages;
+        const uint32_t ph = (j / C::kStages) & 1;
+        const int b = j & 1;
+        const uint32_t pb = (j >> 1) & 1;
+        ok = wait_or_abort(&k_full[st], ph, abort_flag) && wait_or_abort(&s_empty[b], pb ^ 1, abort_flag);
+        if (!ok) break;
+        umma::fence_after_sync();
+        const uint32_t k_addr = base_u32 + C::kKOff + st * C::kTileBytes;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const uint64_t ad = umma::smem_desc_sw128(q_addr + (ks >> 2) * C::kBlockBytes + (ks & 3) * 32, 16, 1024);
+          const uint64_t bd = umma::smem_desc_sw128(k_addr + (ks >> 2) * C::kBlockBytes + (ks & 3) * 32, 16, 1024);
+          umma::mma_f16_ss(tmem + b * 128, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
+        }
+        umma::commit(&s_full[b]);
+        if (j >= 1) ok = issue_pv(j - 1);
+      }
+      if (ok) ok = issue_pv(n_kv - 1);
+      if (!ok) report(p.status);
+      // Drain: every MMA issued so far completes before TMEM is released.
+      umma::commit(final_bar);
+      ptx::mbar_wait(final_bar, 0, 100000000ull);
+    }
+    __syncwarp();
+  } else {
+    // =========================== softmax warps ==============================
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = quarter * 32 + lane;
+    const int q_pos = mtile * 128 + r;
+    const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+    const float sl2 = p.scale_log2;
+    float o[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) o[i] = 0.f;
+    float m = -INFINITY, l = 0.f, corr_prev = 1.f;
+    bool ok = true;
+
+    auto accumulate = [&](int i, float cf) -> bool {
+      const int b = i & 1;
+      const uint32_t pb = (i >> 1) & 1;
+      bool w = wait_or_abort(&o_full[b], pb, abort_flag);
+      w = __all_sync(0xffffffffu, w);
+      if (!w) return false;
+      umma::fence_after_sync();
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float t[32];
+        umma::ld_32x32b_x32(t_lane + C::kOCol + b * D + c * 32, t);
+        umma::ld_wait();
+#pragma unroll
+        for (int x = 0; x < 32; ++x) o[c * 32 + x] = fmaf(o[c * 32 + x], cf, t[x]);
+      }
+      umma::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&o_empty[b]);
+      return true;
+    };
+
+    for (int j = 0; j < n_kv; ++j) {
+      const int b = j & 1;
+      const uint32_t pb = (j >> 1) & 1;
+      ok = wait_or_abort(&s_full[b], pb, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      umma::fence_after_sync();
+      const int kv0 = j * 128;
+      // keys visible to this row: [0, lim)
+      const int lim = p.causal ? min(q_pos + 1, L) : L;
+      const int lim_rel = lim - kv0;  // may be <= 0 only for rows past the prompt end
+      // pass 1: row max of the raw scores
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float s[32];
+        umma::ld_32x32b_x32(t_lane + b * 128 + c * 32, s);
+        umma::ld_wait();
+#pragma unroll
+        for (int x = 0; x < 32; ++x) mx = fmaxf(mx, (c * 32 + x < lim_rel) ? s[x] : -INFINITY);
+      }
+      float m_new = fmaxf(m, mx * sl2);
+      if (m_new == -INFINITY) m_new = 0.f;  // a row with no visible key (past the prompt end)
+      const float corr = exp2f(m - m_new);
+      // pass 2: probabilities -> P (fp16/bf16, swizzled K-major) and the row sum
+      float sum = 0.f;
+      uint8_t* prow = base + C::kPOff + b * C::kPBytes;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float s[32];
+        umma::ld_32x32b_x32(t_lane + b * 128 + c * 32, s);
+        umma::ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int x = 0; x < 16; ++x) {
+          const int col = c * 32 + 2 * x;
+          const float p0 = col < lim_rel ? exp2f(fmaf(s[2 * x], sl2, -m_new)) : 0.f;
+          const float p1 = col + 1 < lim_rel ? exp2f(fmaf(s[2 * x + 1], sl2, -m_new)) : 0.f;
+          sum += p0 + p1;
+          pk[x] = DT<T>::pack2(p0, p1);
+        }
+        const int kb = c >> 1, chunk0 = (c & 1) * 4;
+#pragma unroll
+        for (int t4 = 0; t4 < 4; ++t4) {
+          const uint32_t off = kb * C::kBlockBytes + r * 128 + ((((chunk0 + t4) ^ (r & 7)) & 7) << 4);
+          *reinterpret_cast<uint4*>(prow + off) = make_uint4(pk[4 * t4], pk[4 * t4 + 1], pk[4 * t4 + 2], pk[4 * t4 + 3]);
+        }
+      }
+      umma::fence_before_sync();
+      umma::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        ptx::mbar_arrive(&s_empty[b]);
+        ptx::mbar_arrive(&p_full[b]);
+      }
+      l = l * corr + sum;
+      m = m_new;
+      if (j >= 1 && !(ok = accumulate(j - 1, corr_prev))) break;
+      corr_prev = corr;
+    }
+    if (ok) ok = accumulate(n_kv - 1, corr_prev);
+    if (!ok) {
+      report(p.status);
+    } else if (q_pos < L) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      T* orow = reinterpret_cast<T*>(p.out) + ((size_t)(s0 + q_pos) * p.n_heads + h) * D;
+#pragma unroll
+      for (int c8 = 0; c8 < D / 8; ++c8) {
+        uint4 v;
+        v.x = DT<T>::pack2(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv);
+        v.y = DT<T>::pack2(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv);
+        v.z = DT<T>::pack2(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv);
+        v.w = DT<T>::pack2(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv);
+        *reinterpret_cast<uint4*>(orow + c8 * 8) = v;
+      }
+    }
+  }
+
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    umma::fence_after_sync();
+    umma::tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+// -----------------------------------------------------------------------------
+// SIMT prefill (any dtype, head_dim 32/64/128): one warp handles four query
+// rows, lanes split head_dim, fp32 online softmax.  Also does the paged write.
+// -----------------------------------------------------------------------------
+constexpr int kSimtRows = 16;  // query rows per CTA (4 warps x 4 rows)
+
+template <typename T, int D>
+__global__ void __launch_bounds__(128) flash_prefill_simt_kernel(const PrefillParams p) {
+  constexpr int E = D / 32;  // elements per lane
+  const int seq = blockIdx.z, h = blockIdx.y;
+  const int s0 = p.cu_seqlens[seq];
+  const int L = p.cu_seqlens[seq + 1] - s0;
+  const int row0 = blockIdx.x * kSimtRows;
+  if (row0 >= L) return;
+  const int kvh = h / p.group;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const T* q = reinterpret_cast<const T*>(p.q);
+  const T* k = reinterpret_cast<const T*>(p.k);
+  const T* v = reinterpret_cast<const T*>(p.v);
+
+  if (p.slot_mapping != nullptr && (h % p.group) == 0) {
+    const long long n_slots = (long long)p.num_blocks * p.block_size;
+    T* kc = reinterpret_cast<T*>(p.k_cache);
+    T* vc = reinterpret_cast<T*>(p.v_cache);
+    const int rows = min(kSimtRows, L - row0);
+    for (int i = threadIdx.x; i < rows * D; i += blockDim.x) {
+      const int rr = i / D, d = i % D;
+      const int tok = s0 + row0 + rr;
+      const long long slot = p.slot_mapping[tok];
+      if (slot < 0 || slot >= n_slots) continue;
+      const size_t src = ((size_t)tok * p.n_kv_heads + kvh) * D + d;
+      const size_t dst = ((size_t)slot * p.n_kv_heads + kvh) * D + d;
+      kc[dst] = k[src];
+      vc[dst] = v[src];
+    }
+  }
+
+  float qr[4][E], acc[4][E], m[4], l[4];
+  int qp[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    qp[i] = row0 + warp * 4 + i;
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      acc[i][e] = 0.f;
+      qr[i][e] = qp[i] < L ? DT<T>::to_f(q[((size_t)(s0 + qp[i]) * p.n_heads + h) * D + lane + 32 * e]) : 0.f;
+    }
+  }
+  const int last = qp[3] < L ? qp[3] : L - 1;
+  const int kv_end = p.causal ? last + 1 : L;
+  for (int t = 0; t < kv_end; ++t) {
+    float kr[E], vr[E];
+    const size_t off = ((size_t)(s0 + t) * p.n_kv_heads + kvh) * D;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      kr[e] = DT<T>::to_f(k[off + lane + 32 * e]);
+      vr[e] = DT<T>::to_f(v[off + lane + 32 * e]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) s = fmaf(qr[i][e], kr[e], s);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      const bool vis = qp[i] < L && (!p.causal || t <= qp[i]);
+      if (vis) {
+        const float s2 = s * p.scale_log2;
+        const float mn = fmaxf(m[i], s2);
+        const float corr = exp2f(m[i] - mn);
+        const float pr = exp2f(s2 - mn);
+        l[i] = l[i] * corr + pr;
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[i][e] = fmaf(acc[i][e], corr, pr * vr[e]);
+        m[i] = mn;
+      }
+    }
+  }
+  T* out = reinterpret_cast<T*>(p.out);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (qp[i] >= L) continue;
+    const float inv = l[i] > 0.f ? 1.f / l[i] : 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e)
+      out[((size_t)(s0 + qp[i]) * p.n_heads + h) * D + lane + 32 * e] = DT<T>::from_f(acc[i][e] * inv);
+  }
+}
+
+// -----------------------------------------------------------------------------
+// host side
+// -----------------------------------------------------------------------------
+int encode_rows_map(CUtensorMap* m, const void* ptr, CUtensorMapDataType tdt, int D, int heads, int total) {
+  tvk::EncodeTiledFn encode = tvk::encode_tiled_fn();
+  if (!encode) {
+    tvk::set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return TVK_ERR_CUDA;
+  }
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)heads, (cuuint64_t)total};
+  cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)heads * D * 2};
+  cuuint32_t box[3] = {64u, 1u, 128u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = encode(m, tdt, 3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    tvk::set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return TVK_ERR_CUDA;
+  }
+  return TVK_OK;
+}
+
+template <typename T, int D>
+int launch_tc(const PrefillParams& p, int total, CUtensorMapDataType tdt, cudaStream_t stream) {
+  using C = PfCfg<D>;
+  CUtensorMap tq, tk, tv;
+  int rc = encode_rows_map(&tq, p.q, tdt, D, p.n_heads, total);
+  if (rc == TVK_OK) rc = encode_rows_map(&tk, p.k, tdt, D, p.n_kv_heads, total);
+  if (rc == TVK_OK) rc = encode_rows_map(&tv, p.v, tdt, D, p.n_kv_heads, total);
+  if (rc != TVK_OK) return rc;
+  auto kern = flash_prefill_tc_kernel<T, D>;
+  static unsigned long long attr_mask = 0;
+  int dev = 0;
+  TVK_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev >= 64 || !(attr_mask & (1ull << dev))) {
+    TVK_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
+    if (dev < 64) attr_mask |= 1ull << dev;
+  }
+  dim3 grid(p.n_mtiles, p.n_heads, p.n_seqs);
+  kern<<<grid, 192, C::kSmemBytes, stream>>>(p, tq, tk, tv);
+  TVK_CHECK_LAUNCH("flash_prefill_tc");
+  return TVK_OK;
+}
+
+template <typename T>
+int launch_simt(const PrefillParams& p, int max_seqlen, cudaStream_t stream) {
+  dim3 grid((max_seqlen + kSimtRows - 1) / kSimtRows, p.n_heads, p.n_seqs);
+  switch (p.head_dim) {
+    case 32: flash_prefill_simt_kernel<T, 32><<<grid, 128, 0, stream>>>(p); break;
+    case 64: flash_prefill_simt_kernel<T, 64><<<grid, 128, 0, stream>>>(p); break;
+    default: flash_prefill_simt_kernel<T, 128><<<grid, 128, 0, stream>>>(p); break;
+  }
+  TVK_CHECK_LAUNCH("flash_prefill_simt");
+  return TVK_OK;
+}
+
+}  // namespace
+
+extern "C" int tvk_flash_prefill_attention(const void* q, const void* k, const void* v, void* out,
+                                           const int32_t* cu_seqlens, int n_seqs, int max_seqlen, int total_tokens,
+                                           int n_heads, int n_kv_heads, int head_dim, int causal, int dtype,
+                                           const int64_t* slot_mapping, void* k_cache, void* v_cache, int num_blocks,
+                                           int block_size, void* workspace, size_t workspace_bytes, void* stream) {
+  TVK_CHECK_ARG(n_seqs >= 0 && total_tokens >= 0 && max_seqlen >= 0, "negative size");
+  if (n_seqs == 0 || total_tokens == 0 || max_seqlen == 0) return TVK_OK;
+  TVK_CHECK_ARG(q && k && v && out && cu_seqlens, "null pointer argument");
+  TVK_CHECK_ARG(n_seqs <= 65535 && n_heads <= 65535, "n_seqs and n_heads must be <= 65535");
+  TVK_CHECK_ARG(n_heads > 0 && n_kv_heads > 0 && n_heads % n_kv_heads == 0,
+                "n_heads (%d) must be a positive multiple of n_kv_heads (%d)", n_heads, n_kv_heads);
+  TVK_CHECK_ARG(dtype == TVK_DTYPE_F32 || dtype == TVK_DTYPE_F16 || dtype == TVK_DTYPE_BF16, "unknown dtype %d",
+                dtype);
+  if (head_dim != 32 && head_dim != 64 && head_dim != 128) {
+    tvk::set_error("head_dim %d unsupported (32, 64 or 128)", head_dim);
+    return TVK_ERR_UNSUPPORTED;
+  }
+  TVK_CHECK_ARG((uintptr_t)q % 16 == 0 && (uintptr_t)k % 16 == 0 && (uintptr_t)v % 16 == 0 &&
+                    (uintptr_t)out % 16 == 0,
+                "q, k, v and out must be 16-byte aligned");
+  if (slot_mapping) {
+    TVK_CHECK_ARG(k_cache && v_cache && num_blocks > 0 && block_size > 0,
+                  "a slot mapping needs k_cache, v_cache, num_blocks and block_size");
+    TVK_CHECK_ARG((uintptr_t)k_cache % 16 == 0 && (uintptr_t)v_cache % 16 == 0, "caches must be 16-byte aligned");
+  }
+  PrefillParams p{};
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.out = out;
+  p.cu_seqlens = cu_seqlens;
+  p.slot_mapping = slot_mapping;
+  p.k_cache = k_cache;
+  p.v_cache = v_cache;
+  p.status = workspace && workspace_bytes >= sizeof(int) ? reinterpret_cast<int*>(workspace) : nullptr;
+  p.n_seqs = n_seqs;
+  p.n_heads = n_heads;
+  p.n_kv_heads = n_kv_heads;
+  p.group = n_heads / n_kv_heads;
+  p.head_dim = head_dim;
+  p.causal = causal ? 1 : 0;
+  p.num_blocks = num_blocks;
+  p.block_size = block_size;
+  p.n_mtiles = (max_seqlen + 127) / 128;
+  p.scale_log2 = (float)(1.4426950408889634 / sqrt((double)head_dim));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool tc = dtype != TVK_DTYPE_F32 && (head_dim == 64 || head_dim == 128);
+  if (tc) {
+    if (dtype == TVK_DTYPE_F16)
+      return head_dim == 64 ? launch_tc<__half, 64>(p, total_tokens, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, s)
+                            : launch_tc<__half, 128>(p, total_tokens, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, s);
+    return head_dim == 64 ? launch_tc<__nv_bfloat16, 64>(p, total_tokens, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, s)
+                          : launch_tc<__nv_bfloat16, 128>(p, total_tokens, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, s);
+  }
+  switch (dtype) {
+    case TVK_DTYPE_F16: return launch_simt<__half>(p, max_seqlen, s);
+    case TVK_DTYPE_BF16: return launch_simt<__nv_bfloat16>(p, max_seqlen, s);
+    default: return launch_simt<float>(p, max_seqlen, s);
+  }
+}
