@@ -100,10 +100,14 @@ int tvk_paged_decode_attention(const void* q, const void* k_cache, const void* v
  *              also stored at k_cache/v_cache [num_blocks, block_size, n_kv_heads,
  *              head_dim] flat slot slot_mapping[t] (= block * block_size + offset);
  *              negative or out-of-pool slots are skipped.
- *   workspace  optional (>= 4 bytes): its first int is set to 1 if a bounded wait expired.
+ *   workspace  >= tvk_flash_prefill_workspace_size(n_seqs, total_tokens) bytes for the
+ *              tcgen05 path (its work schedule lives there; optional otherwise); its
+ *              first int is set non-zero if a bounded wait expired.
  * fp16/bf16 with head_dim 64 or 128 run on tcgen05 (TMEM accumulators, TMA
- * loads); fp32 and head_dim 32 use a CUDA-core kernel.  Softmax is fp32.
+ * loads, persistent CTAs over a heaviest-first tile schedule built on the
+ * device); fp32 and head_dim 32 use a CUDA-core kernel.  Softmax is fp32.
  */
+size_t tvk_flash_prefill_workspace_size(int n_seqs, int total_tokens);
 int tvk_flash_prefill_attention(const void* q, const void* k, const void* v, void* out,
                                 const int32_t* cu_seqlens, int n_seqs, int max_seqlen, int total_tokens,
                                 int n_heads, int n_kv_heads, int head_dim, int causal, int dtype,

@@ -129,8 +129,8 @@ def flash_prefill_attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Te
         num_blocks, block_size = k_cache.shape[0], k_cache.shape[1]
     if out is None:
         out = torch.empty_like(q)
-    ws = _workspace(dev, 256)
     L = _lib.lib()
+    ws = _workspace(dev, L.tvk_flash_prefill_workspace_size(n_seqs, T))
     rc = L.tvk_flash_prefill_attention(
         _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(out), _lib.ptr(cu_seqlens), n_seqs, int(max_seqlen), T,
         Hq, Hkv, D, 1 if causal else 0, _lib.dtype_code(q), _lib.ptr(slot_mapping), _lib.ptr(k_cache),
