@@ -345,73 +345,69 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
         umma::fence_after_sync();
         const int lim_rel = lim - j * 128;  // keys [0, lim_rel) of this tile are visible
         const uint32_t s_addr = t_lane + sb * 128;
-        // pass 1: row max of the visible raw scores
+        // pass 1: row max of the visible raw scores (two 64-column loads per wait)
         float mx = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float s[32];
-          umma::ld_32x32b_x32(s_addr + c * 32, s);
+        for (int c = 0; c < 4; c += 2) {
+          float s[64];
+          umma::ld_32x32b_x32(s_addr + c * 32, *reinterpret_cast<float(*)[32]>(&s[0]));
+          umma::ld_32x32b_x32(s_addr + c * 32 + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
           umma::ld_wait();
           if (lim_rel >= 128) {
 #pragma unroll
-            for (int x = 0; x < 32; ++x) mx = fmaxf(mx, s[x]);
+            for (int x = 0; x < 64; ++x) mx = fmaxf(mx, s[x]);
           } else {
 #pragma unroll
-            for (int x = 0; x < 32; ++x) mx = fmaxf(mx, c * 32 + x < lim_rel ? s[x] : -INFINITY);
+            for (int x = 0; x < 64; ++x) mx = fmaxf(mx, c * 32 + x < lim_rel ? s[x] : -INFINITY);
           }
         }
         float m_cand = fmaxf(m, mx * sl2);
         if (m_cand == -INFINITY) m_cand = 0.f;  // no visible key (cannot happen for a live tile)
-        if (j > 0) {
-          // P is single-buffered and O is rescaled in place: the previous P.V must be done.
+        // P is single-buffered and O is rescaled in place, so the previous P.V must be
+        // complete before either is touched; wait for it as late as possible.
+        bool pv_waited = (j == 0);
+        if (j == 0) {
+          m = m_cand;
+        } else if (__any_sync(0xffffffffu, m_cand > m + 8.f)) {
+          // Lazy rescale: the stale max is kept unless the new one is 2^8 larger.
           ok = __all_sync(0xffffffffu, wait_or_abort(pv_done, pv_it & 1, abort_flag));
           if (!ok) break;
           ++pv_it;
-          // Lazy rescale: keep the stale max unless the new one is 2^8 larger.
-          if (__any_sync(0xffffffffu, m_cand > m + 8.f)) {
-            umma::fence_after_sync();
-            const float corr = ex2(m - m_cand);
+          pv_waited = true;
+          umma::fence_after_sync();
+          const float corr = ex2(m - m_cand);
 #pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
-              float o[32];
-              umma::ld_32x32b_x32(t_lane + C::kOCol + c * 32, o);
-              umma::ld_wait();
+          for (int c = 0; c < D / 32; ++c) {
+            float o[32];
+            umma::ld_32x32b_x32(t_lane + C::kOCol + c * 32, o);
+            umma::ld_wait();
 #pragma unroll
-              for (int x = 0; x < 32; ++x) o[x] *= corr;
-              umma::st_32x32b_x32(t_lane + C::kOCol + c * 32, o);
-            }
-            umma::st_wait();
-            l *= corr;
-            m = m_cand;
+            for (int x = 0; x < 32; ++x) o[x] *= corr;
+            umma::st_32x32b_x32(t_lane + C::kOCol + c * 32, o);
           }
-        } else {
+          umma::st_wait();
+          l *= corr;
           m = m_cand;
         }
-        // pass 2: P = 2^(s*scale - m) -> fp16/bf16, swizzled K-major rows of 128 keys
+        // pass 2: P = 2^(s*scale - m) packed to fp16/bf16 in registers (64 columns per load)
         float sum = 0.f;
+        uint32_t pk[64];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          float s[32];
-          umma::ld_32x32b_x32(s_addr + c * 32, s);
+        for (int hf = 0; hf < 2; ++hf) {
+          float s[64];
+          umma::ld_32x32b_x32(s_addr + hf * 64, *reinterpret_cast<float(*)[32]>(&s[0]));
+          umma::ld_32x32b_x32(s_addr + hf * 64 + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
           umma::ld_wait();
           if (lim_rel < 128) {
 #pragma unroll
-            for (int x = 0; x < 32; ++x) s[x] = c * 32 + x < lim_rel ? s[x] : -INFINITY;
+            for (int x = 0; x < 64; ++x) s[x] = hf * 64 + x < lim_rel ? s[x] : -INFINITY;
           }
-          uint32_t pk[16];
 #pragma unroll
-          for (int x = 0; x < 16; ++x) {
+          for (int x = 0; x < 32; ++x) {
             const float p0 = ex2(fmaf(s[2 * x], sl2, -m));
             const float p1 = ex2(fmaf(s[2 * x + 1], sl2, -m));
             sum += p0 + p1;
-            pk[x] = DT<T>::pack2(p0, p1);
-          }
-          const int kb = c >> 1, chunk0 = (c & 1) * 4;
-#pragma unroll
-          for (int t4 = 0; t4 < 4; ++t4) {
-            const uint32_t off = kb * C::kBlockBytes + r * 128 + ((((chunk0 + t4) ^ (r & 7)) & 7) << 4);
-            *reinterpret_cast<uint4*>(prow + off) =
-                make_uint4(pk[4 * t4], pk[4 * t4 + 1], pk[4 * t4 + 2], pk[4 * t4 + 3]);
+            pk[hf * 32 + x] = DT<T>::pack2(p0, p1);
           }
         }
         // S has been read: hand the TMEM buffer back to the MMA warp.
@@ -419,6 +415,18 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&s_empty[sb]);
         ++s_it;
+        if (!pv_waited) {
+          ok = __all_sync(0xffffffffu, wait_or_abort(pv_done, pv_it & 1, abort_flag));
+          if (!ok) break;
+          ++pv_it;
+        }
+        // P -> shared memory, swizzled K-major rows of 128 keys
+#pragma unroll
+        for (int c8 = 0; c8 < 16; ++c8) {
+          const int kb = c8 >> 3;
+          const uint32_t off = kb * C::kBlockBytes + r * 128 + ((((c8 & 7) ^ (r & 7)) & 7) << 4);
+          *reinterpret_cast<uint4*>(prow + off) = make_uint4(pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
+        }
         l += sum;
         umma::fence_before_sync();
         umma::fence_proxy_async_smem();
