@@ -115,6 +115,74 @@ int tvk_flash_prefill_attention(const void* q, const void* k, const void* v, voi
                                 int num_blocks, int block_size,
                                 void* workspace, size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Per-layer ops around the attention (fp32 arithmetic, one rounding to dtype;
+ * pointers 16-byte aligned, contiguous rows unless a stride is given).
+ * ------------------------------------------------------------------------ */
+
+/*
+ * RMSNorm, RMSNorm.__call__ (tinyvllm/model/llama.py:21-23):
+ *   out = s * rsqrt(mean(s^2) + eps) * weight,  s = x            (residual == NULL)
+ *                                               s = x + residual (rounded to dtype; also
+ *                                               stored to residual_out -- the residual add of
+ *                                               TransformerBlock.__call__, llama.py:247-250)
+ * x, residual, residual_out, out [rows, dim]; weight [dim].  dim <= 2048 * (16 / sizeof(dtype)).
+ */
+int tvk_rms_norm(const void* x, const void* residual, void* residual_out, const void* weight, void* out,
+                 int rows, int dim, float eps, int dtype, void* stream);
+
+/*
+ * In-place interleaved-pair RoPE on q [n_tokens, n_heads, head_dim] and
+ * k [n_tokens, n_kv_heads, head_dim], apply_rope (llama.py:34-55):
+ *   (x[2i], x[2i+1]) -> (x0 c - x1 s, x0 s + x1 c),  c/s = table[positions[t], i]
+ * cos_table / sin_table fp32 [max_pos, head_dim / 2] (precompute_freqs_cis, llama.py:26-31).
+ */
+int tvk_rope(void* q, void* k, const float* cos_table, const float* sin_table, const int32_t* positions,
+             int n_tokens, int n_heads, int n_kv_heads, int head_dim, int max_pos, int dtype, void* stream);
+
+/*
+ * tvk_rope, then the roped k rows and the v rows [n_tokens, n_kv_heads, head_dim]
+ * stored into k_cache / v_cache [num_blocks, block_size, n_kv_heads, head_dim] at
+ * flat slot slots[t] (negative or out-of-pool slots skipped): RoPE fused with the
+ * K/V write of llama.py:322-323 + 381-386 / 188-209.
+ */
+int tvk_rope_write_kv(void* q, void* k, const void* v, const float* cos_table, const float* sin_table,
+                      const int32_t* positions, const int64_t* slots, void* k_cache, void* v_cache,
+                      int n_tokens, int n_heads, int n_kv_heads, int head_dim, int max_pos,
+                      int num_blocks, int block_size, int dtype, void* stream);
+
+/*
+ * k/v rows [n_tokens, n_kv_heads, head_dim] -> paged slots, KVCache.write_kv
+ * (core/kv_cache.py:34-38); one launch for a whole decode batch replaces the
+ * reference's per-sequence, per-layer writes (llama.py:381-386).
+ */
+int tvk_write_kv_slots(const void* k, const void* v, const int64_t* slots, void* k_cache, void* v_cache,
+                       int n_tokens, int n_kv_heads, int head_dim, int num_blocks, int block_size,
+                       int dtype, void* stream);
+
+/*
+ * SwiGLU gate of FeedForward.__call__ (llama.py:220-221):
+ *   out[r, c] = silu(a[r, c]) * b[r, c]   (silu rounded to dtype before the product)
+ * Row strides in elements (a packed gate|up GEMM output: a = base, b = base + cols,
+ * a_stride = b_stride = 2 * cols).
+ */
+int tvk_silu_mul(const void* a, const void* b, void* out, int rows, int cols, long long a_stride,
+                 long long b_stride, long long out_stride, int dtype, void* stream);
+
+/*
+ * Embedding row gather (llama.py:276,310): out[t] = table[tokens[t]].  Ids outside
+ * [0, vocab) give zero rows and set *status = 3 (status may be NULL).
+ */
+int tvk_embedding(const void* table, const int32_t* tokens, void* out, int n_tokens, int dim, int vocab,
+                  int dtype, int* status, void* stream);
+
+/*
+ * Greedy pick (core/sampling.py:133-134): out[r] = argmax over logits[r, :vocab],
+ * first index on ties, compared in fp32 after conversion from dtype.
+ */
+int tvk_argmax(const void* logits, int32_t* out, int rows, int vocab, long long row_stride, int dtype,
+               void* stream);
+
 /*
  * Paged-decode attention that allocates nothing (no counterpart in the
  * reference, which lets tinygrad allocate its temporaries).

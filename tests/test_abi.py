@@ -42,6 +42,24 @@ def test_python_binding_covers_header(lib):
     assert set(_declared_symbols()) <= set(_lib.SIGNATURES), "ctypes prototypes missing for some exports"
 
 
+def _declared_arity():
+    arity = {}
+    for h in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        for name, params in re.findall(r"\b(tvk_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", text, flags=re.S):
+            params = params.strip()
+            arity[name] = 0 if params in ("", "void") else params.count(",") + 1
+    return arity
+
+
+def test_binding_argument_counts_match_header():
+    from tinyvllm_b200 import _lib
+    arity = _declared_arity()
+    assert arity, "no declarations parsed"
+    for name, n in arity.items():
+        assert len(_lib.SIGNATURES[name][1]) == n, f"{name}: header has {n} parameters"
+
+
 def test_abi_version(lib):
     assert lib.tvk_abi_version() == 1
 

@@ -31,6 +31,13 @@ SIGNATURES = {
     ),
     "tvk_selftest_umma_gemm": (_c_int, [_c_void] * 3 + [_c_int] * 4 + [_c_void, _c_void]),
     "tvk_paged_decode_attention_noalloc": (_c_int, [_c_void] * 6 + [_c_int] * 9 + [_c_void]),
+    "tvk_rms_norm": (_c_int, [_c_void] * 5 + [_c_int, _c_int, _c_float, _c_int, _c_void]),
+    "tvk_rope": (_c_int, [_c_void] * 5 + [_c_int] * 6 + [_c_void]),
+    "tvk_rope_write_kv": (_c_int, [_c_void] * 9 + [_c_int] * 8 + [_c_void]),
+    "tvk_write_kv_slots": (_c_int, [_c_void] * 5 + [_c_int] * 6 + [_c_void]),
+    "tvk_silu_mul": (_c_int, [_c_void] * 3 + [_c_int, _c_int, _c_int64, _c_int64, _c_int64, _c_int, _c_void]),
+    "tvk_embedding": (_c_int, [_c_void] * 3 + [_c_int] * 4 + [_c_void, _c_void]),
+    "tvk_argmax": (_c_int, [_c_void] * 2 + [_c_int, _c_int, _c_int64, _c_int, _c_void]),
     "tvk_flash_prefill_workspace_size": (_c_size, [_c_int] * 2),
     "tvk_flash_prefill_attention": (
         _c_int,
