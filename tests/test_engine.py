@@ -1,0 +1,189 @@
+"""End-to-end engine on the kernels vs the CPU oracle engine: identical greedy
+token streams (GPU).
+
+The oracle (``oracle/engine.py``) replays the reference's step order exactly:
+one prompt per prefill with chunked K/V writes, decode attention over the cache
+before the step's own K/V is written, tables padded to 64 blocks with block 0,
+LIFO block reuse after sequences finish.  A tight pool forces reuse, so stale
+K/V in reused blocks is read exactly as the reference reads it.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.engine import OracleEngine, OracleLlama
+
+pytestmark = pytest.mark.gpu
+
+
+def _requests(seed, n, vocab, len_lo, len_hi, tok_lo, tok_hi):
+    rng = np.random.default_rng(seed)
+    prompts = [rng.integers(0, vocab, size=int(rng.integers(len_lo, len_hi + 1))).tolist() for _ in range(n)]
+    max_toks = rng.integers(tok_lo, tok_hi + 1, size=n).tolist()
+    return prompts, max_toks
+
+
+def _run_product(model, prompts, max_toks, **kw):
+    from tinyvllm_b200.engine import LLMEngine, SamplingParams
+    eng = LLMEngine(model, **kw)
+    outs, i = {}, 0
+    while i < len(prompts) or eng.has_unfinished():
+        for _ in range(2):                 # staggered arrivals: two new requests per step
+            if i < len(prompts):
+                eng.add_request(prompts[i], SamplingParams(temperature=0.0, max_tokens=max_toks[i]))
+                i += 1
+        for o in eng.step():
+            outs[o.request_id] = o.tokens
+    return outs, eng
+
+
+def _run_oracle(model, prompts, max_toks, max_batch_size, num_blocks, num_scheduler_steps=1, with_gaps=False):
+    c = model.config
+    om = OracleLlama(model.numpy_weights(), c.n_layers, c.n_heads, c.n_kv_heads, c.head_dim, c.norm_eps,
+                     c.rope_theta, c.max_seq_len)
+    eng = OracleEngine(om, max_batch_size, num_blocks, 16, num_scheduler_steps)
+    i = 0
+    while i < len(prompts) or eng.has_unfinished():
+        for _ in range(2):
+            if i < len(prompts):
+                eng.add_request(prompts[i], max_toks[i])
+                i += 1
+        eng.step()
+    return (eng.outputs, eng.gaps) if with_gaps else eng.outputs
+
+
+def _tiny(dtype, dim, heads, kv_heads, seed=0, max_seq_len=256):
+    from tinyvllm_b200.model import Llama, LlamaConfig
+    cfg = LlamaConfig(dim=dim, n_layers=2, n_heads=heads, n_kv_heads=kv_heads, vocab_size=97, hidden_dim=2 * dim,
+                      max_seq_len=max_seq_len, dtype=dtype)
+    # std 0.25 keeps the logits spread wide enough that float rounding cannot flip the argmax
+    return Llama(cfg, device="cuda", seed=seed, init_std=0.25)
+
+
+@pytest.mark.parametrize("steps", [1, 3])
+def test_greedy_streams_match_oracle_fp32(cuda, steps):
+    model = _tiny("float32", 128, 4, 2)
+    prompts, max_toks = _requests(1, 7, 97, 3, 40, 5, 25)
+    got, eng = _run_product(model, prompts, max_toks, max_batch_size=4, num_blocks=24, num_scheduler_steps=steps)
+    exp = _run_oracle(model, prompts, max_toks, 4, 24, steps)
+    assert got == exp
+    assert eng.block_manager.get_num_free_blocks() == 24
+
+
+@pytest.mark.parametrize("dtype,tol", [("float16", 0.5), ("bfloat16", 1.5)])
+def test_half_precision_engine_tracks_oracle(cuda, dtype, tol):
+    """head_dim 64 in fp16 / bf16 runs the TMA/mma decode kernel and the tcgen05 prefill
+    kernel.  Half-precision activations move these logits (std ~4) by ~0.2 (fp16) /
+    ~0.6 (bf16) against the fp32 oracle, enough to flip near-ties, so the streams are
+    teacher-forced: the product engine is fed the oracle's tokens and every logit row
+    it produces must lie within ``tol`` of the oracle's, and its own argmax must equal
+    the oracle's token wherever the oracle's top-1/top-2 margin exceeds 2 * tol.
+    Block reuse is on (a tight pool), as in the fp32 stream test.
+    """
+    from tinyvllm_b200.engine import LLMEngine, SamplingParams
+    model = _tiny(dtype, 256, 4, 2, seed=3)
+    prompts, max_toks = _requests(2, 6, 97, 3, 150, 4, 16)
+    exp, gaps = _run_oracle(model, prompts, max_toks, 3, 40, with_gaps=True)
+    c = model.config
+    oracle_logits = {}
+    om = OracleLlama(model.numpy_weights(), c.n_layers, c.n_heads, c.n_kv_heads, c.head_dim, c.norm_eps,
+                     c.rope_theta, c.max_seq_len)
+    oe = OracleEngine(om, 3, 40)
+    i = 0
+    while i < len(prompts) or oe.has_unfinished():
+        for _ in range(2):
+            if i < len(prompts):
+                oe.add_request(prompts[i], max_toks[i])
+                i += 1
+        oe.step()
+    oracle_logits = oe.logits
+
+    class Forced(LLMEngine):
+        recorded = {}
+
+        def _sample(self, logits, seqs):
+            rows = logits.float().cpu().numpy()
+            out = []
+            for s, row in zip(seqs, rows):
+                k = len(s.output_tokens)
+                self.recorded.setdefault(s.request_id, []).append(row)
+                out.append(exp[s.request_id][k])
+            return out
+
+    eng = Forced(model, max_batch_size=3, num_blocks=40)
+    i = 0
+    while i < len(prompts) or eng.has_unfinished():
+        for _ in range(2):
+            if i < len(prompts):
+                eng.add_request(prompts[i], SamplingParams(max_tokens=max_toks[i]))
+                i += 1
+        eng.step()
+    n_checked = 0
+    for rid in exp:
+        got_rows, exp_rows = Forced.recorded[rid], oracle_logits[rid]
+        assert len(got_rows) == len(exp_rows)
+        for k, (g, e) in enumerate(zip(got_rows, exp_rows)):
+            assert np.abs(g - e).max() <= tol, f"request {rid} token {k}: logits off by {np.abs(g - e).max()}"
+            if gaps[rid][k] > 2 * tol:
+                assert int(np.argmax(g)) == exp[rid][k]
+                n_checked += 1
+    assert n_checked > 0
+
+
+def test_context_beyond_64_blocks_is_truncated_like_the_reference(cuda):
+    """Decode tables are cut at 64 blocks (1024 tokens) in the reference engine."""
+    model = _tiny("float32", 128, 4, 2, seed=4, max_seq_len=1024)
+    prompts = [np.random.default_rng(5).integers(0, 97, size=1030).tolist()]
+    got, _ = _run_product(model, prompts, [6], max_batch_size=1, num_blocks=80)
+    exp = _run_oracle(model, prompts, [6], 1, 80)
+    assert got == exp
+
+
+def test_append_first_mode_sees_its_own_key(cuda):
+    """append_first differs from the reference ordering only in what the new query sees."""
+    from tinyvllm_b200.engine import LLMEngine, SamplingParams
+    model = _tiny("float32", 128, 4, 2, seed=6)
+    prompts, max_toks = _requests(7, 3, 97, 5, 30, 8, 8)
+    a, _ = _run_product(model, prompts, max_toks, max_batch_size=3, num_blocks=20, kv_order="append_first")
+    r, _ = _run_product(model, prompts, max_toks, max_batch_size=3, num_blocks=20)
+    assert set(a) == set(r) and all(len(a[k]) == len(r[k]) for k in a)
+    assert all(a[k][0] == r[k][0] for k in a)   # the prefill token does not depend on the decode order
+
+
+def test_engine_api(cuda):
+    from tinyvllm_b200.engine import LLMEngine, SamplingParams, TokenIdTokenizer, generate_batch
+    model = _tiny("float32", 128, 4, 2, seed=8)
+    eng = LLMEngine(model, max_batch_size=2, num_blocks=16)
+    with pytest.raises(ValueError, match="greedy"):
+        eng.add_request([1, 2, 3], SamplingParams(temperature=1.0))
+    rid = eng.add_request([1, 2, 3], SamplingParams(max_tokens=4))
+    with pytest.raises(ValueError, match="already exists"):
+        eng.add_request([4], request_id=rid)
+    eng.add_request([5, 6], SamplingParams(max_tokens=4))
+    eng.add_request([7, 8, 9], SamplingParams(max_tokens=4))
+    assert eng.abort_request(2) is True and eng.abort_request(99) is False
+    outs = list(eng.run())
+    assert sorted(o.request_id for o in outs) == [0, 1]
+    assert all(len(o.tokens) == 4 and o.finish_reason == "length" for o in outs)
+    assert eng.block_manager.get_num_free_blocks() == 16
+    texts = generate_batch(LLMEngine(model, max_batch_size=4, num_blocks=16), [[1, 2], [3, 4, 5]],
+                           SamplingParams(max_tokens=3))
+    assert len(texts) == 2 and all(len(t.split()) == 3 for t in texts)
+    # eos stops a stream early
+    first = LLMEngine(model, max_batch_size=1, num_blocks=16)
+    first.add_request([1, 2, 3], SamplingParams(max_tokens=5))
+    tok0 = list(first.run())[0].tokens[0]
+    e2 = LLMEngine(model, TokenIdTokenizer(eos_id=tok0), max_batch_size=1, num_blocks=16)
+    e2.add_request([1, 2, 3], SamplingParams(max_tokens=5))
+    out = list(e2.run())[0]
+    assert out.tokens == [tok0] and out.finish_reason == "eos"
+
+
+def test_out_of_blocks_raises_the_reference_error(cuda):
+    from tinyvllm_b200.engine import LLMEngine, SamplingParams
+    model = _tiny("float32", 128, 4, 2, seed=9)
+    eng = LLMEngine(model, max_batch_size=2, num_blocks=2)
+    eng.add_request(list(range(40)), SamplingParams(max_tokens=2))
+    with pytest.raises(RuntimeError, match="Out of KV cache memory!"):
+        eng.step()

@@ -1,0 +1,234 @@
+"""Llama forward passes built on the sm_100a kernels.
+
+``Llama`` restates ``tinyvllm/model/llama.py:224-388`` for the hot path: the
+decode step (``Llama.create_jit_decode`` / ``Llama.decode``, llama.py:290-388)
+and a ragged prefill of several prompts at once (the reference prefills one
+prompt per call, ``Llama.prefill`` llama.py:266-288; prompts are independent, so
+batching them changes no result).  Every per-token op is one of this
+package's kernels; the projections are plain library GEMMs (``torch.matmul`` on
+cuBLAS) into preallocated buffers.
+
+Weights are random N(0, std) from a seeded device generator (the benchmark
+configurations load no checkpoints) with RMSNorm weights of one (llama.py:19).
+Layout: every projection weight is stored [in, out] so a projection is x @ W.
+
+K/V write order: ``kv_order="reference"`` reproduces the reference decode,
+which attends over the cache *before* the step's own K/V is written
+(llama.py:328-332 then 381-386) with block tables built before the new slot is
+allocated (engine.py:247, llama.py:383); ``"append_first"`` writes the step's
+K/V first, so the query also sees its own key.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import layers
+from .attention import flash_prefill_attention_varlen, paged_decode_attention
+
+_DTYPES = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}
+
+
+@dataclass
+class LlamaConfig:
+    """Fields of ``LlamaConfig`` (tinyvllm/model/weights.py:18-44); ``dtype`` also accepts "bfloat16"."""
+    dim: int = 4096
+    n_layers: int = 32
+    n_heads: int = 32
+    n_kv_heads: Optional[int] = None
+    vocab_size: int = 32000
+    hidden_dim: Optional[int] = None
+    norm_eps: float = 1e-5
+    max_seq_len: int = 2048
+    rope_theta: float = 10000.0
+    dtype: str = "float32"
+
+    def __post_init__(self):
+        self.n_kv_heads = self.n_kv_heads or self.n_heads
+        self.hidden_dim = self.hidden_dim or 4 * self.dim
+        if self.dtype not in _DTYPES:
+            raise ValueError(f"dtype must be one of {sorted(_DTYPES)}")
+
+    @property
+    def head_dim(self) -> int:
+        return self.dim // self.n_heads
+
+    @property
+    def torch_dtype(self) -> torch.dtype:
+        return _DTYPES[self.dtype]
+
+
+def tinyllama_config(dtype: str = "float16") -> LlamaConfig:
+    """TinyLlama-1.1B shapes (benchmark config 4)."""
+    return LlamaConfig(dim=2048, n_layers=22, n_heads=32, n_kv_heads=4, vocab_size=32000, hidden_dim=5632,
+                       norm_eps=1e-5, max_seq_len=2048, rope_theta=10000.0, dtype=dtype)
+
+
+def llama3_8b_config(dtype: str = "bfloat16") -> LlamaConfig:
+    """Llama-3-8B shapes (benchmark config 5)."""
+    return LlamaConfig(dim=4096, n_layers=32, n_heads=32, n_kv_heads=8, vocab_size=128256, hidden_dim=14336,
+                       norm_eps=1e-5, max_seq_len=8192, rope_theta=500000.0, dtype=dtype)
+
+
+@dataclass
+class LayerWeights:
+    attention_norm: torch.Tensor
+    wq: torch.Tensor
+    wk: torch.Tensor
+    wv: torch.Tensor
+    wo: torch.Tensor
+    ffn_norm: torch.Tensor
+    w13: torch.Tensor     # [dim, 2*hidden]: gate (w1) columns then up (w3) columns
+    w2: torch.Tensor
+
+
+class KVCache:
+    """Per-layer K and V pools ``[num_blocks, block_size, n_kv_heads, head_dim]``,
+    zero-initialised (core/kv_cache.py:13-32), as device tensors."""
+
+    def __init__(self, num_layers: int, num_blocks: int, block_size: int, n_kv_heads: int, head_dim: int,
+                 dtype: torch.dtype, device="cuda"):
+        self.num_layers = num_layers
+        self.num_blocks = num_blocks
+        self.block_size = block_size
+        self.n_kv_heads = n_kv_heads
+        self.head_dim = head_dim
+        self.dtype = dtype
+        shape = (num_blocks, block_size, n_kv_heads, head_dim)
+        self.k_cache = [torch.zeros(shape, dtype=dtype, device=device) for _ in range(num_layers)]
+        self.v_cache = [torch.zeros(shape, dtype=dtype, device=device) for _ in range(num_layers)]
+
+    def write_kv(self, layer_idx: int, block_id: int, start_offset: int, k: torch.Tensor, v: torch.Tensor) -> None:
+        """KVCache.write_kv (kv_cache.py:34-38): rows [n, Hkv, D] at ``block_id`` from ``start_offset``."""
+        n = k.shape[0]
+        slots = torch.arange(block_id * self.block_size + start_offset,
+                             block_id * self.block_size + start_offset + n, dtype=torch.int64, device=k.device)
+        layers.write_kv_slots(k.contiguous(), v.contiguous(), slots, self.k_cache[layer_idx], self.v_cache[layer_idx])
+
+    def read_kv_blocks(self, layer_idx: int, block_ids: List[int], context_len: int):
+        """kv_cache.py:40-55 (test helper): [context_len, Hkv, D] gathered from ``block_ids``."""
+        if not block_ids:
+            z = torch.zeros(0, self.n_kv_heads, self.head_dim, dtype=self.dtype, device=self.k_cache[0].device)
+            return z, z.clone()
+        idx = torch.tensor(block_ids, dtype=torch.int64, device=self.k_cache[0].device)
+        k = self.k_cache[layer_idx][idx].reshape(-1, self.n_kv_heads, self.head_dim)
+        v = self.v_cache[layer_idx][idx].reshape(-1, self.n_kv_heads, self.head_dim)
+        return k[:context_len], v[:context_len]
+
+    def get_memory_bytes(self) -> int:
+        return (self.num_layers * self.num_blocks * self.block_size * self.n_kv_heads * self.head_dim * 2
+                * torch.tensor([], dtype=self.dtype).element_size())
+
+
+class Llama:
+    def __init__(self, config: LlamaConfig, device="cuda", seed: int = 0, init_std: float = 0.02):
+        self.config = config
+        self.device = torch.device(device)
+        c = config
+        dt = c.torch_dtype
+        g = torch.Generator(device=self.device).manual_seed(seed)
+
+        def rnd(*shape):
+            return (torch.randn(*shape, generator=g, device=self.device, dtype=torch.float32) * init_std).to(dt)
+
+        D = c.head_dim
+        self.tok_embeddings = rnd(c.vocab_size, c.dim)
+        self.layers: List[LayerWeights] = []
+        for _ in range(c.n_layers):
+            self.layers.append(LayerWeights(
+                attention_norm=torch.ones(c.dim, dtype=dt, device=self.device),
+                wq=rnd(c.dim, c.n_heads * D), wk=rnd(c.dim, c.n_kv_heads * D), wv=rnd(c.dim, c.n_kv_heads * D),
+                wo=rnd(c.n_heads * D, c.dim),
+                ffn_norm=torch.ones(c.dim, dtype=dt, device=self.device),
+                w13=rnd(c.dim, 2 * c.hidden_dim), w2=rnd(c.hidden_dim, c.dim)))
+        self.norm = torch.ones(c.dim, dtype=dt, device=self.device)
+        self.output = rnd(c.dim, c.vocab_size)
+        # precompute_freqs_cis(head_dim, 2 * max_seq_len) as the reference does (llama.py:263-264)
+        self.cos, self.sin = layers.precompute_freqs_cis(D, 2 * c.max_seq_len, c.rope_theta, self.device)
+
+    def numpy_weights(self) -> Dict[str, np.ndarray]:
+        """All weights as float32 numpy arrays (for the CPU oracle)."""
+        f = lambda t: t.float().cpu().numpy()
+        w = {"tok_embeddings": f(self.tok_embeddings), "norm": f(self.norm), "output": f(self.output)}
+        H = self.config.hidden_dim
+        for i, L in enumerate(self.layers):
+            w13 = f(L.w13)
+            w.update({f"l{i}.attention_norm": f(L.attention_norm), f"l{i}.wq": f(L.wq), f"l{i}.wk": f(L.wk),
+                      f"l{i}.wv": f(L.wv), f"l{i}.wo": f(L.wo), f"l{i}.ffn_norm": f(L.ffn_norm),
+                      f"l{i}.w1": w13[:, :H], f"l{i}.w3": w13[:, H:], f"l{i}.w2": f(L.w2)})
+        return w
+
+    # ------------------------------------------------------------------ blocks
+    def _layer_ffn(self, L: LayerWeights, h: torch.Tensor, attn: torch.Tensor, next_norm: torch.Tensor,
+                   T: int) -> torch.Tensor:
+        c = self.config
+        o = torch.matmul(attn.view(T, c.n_heads * c.head_dim), L.wo)
+        x = layers.rms_norm(o, L.ffn_norm, c.norm_eps, residual=h)       # h += o; x = ffn_norm(h)
+        gu = torch.matmul(x, L.w13)
+        a = layers.silu_mul(gu[:, :c.hidden_dim], gu[:, c.hidden_dim:])
+        f = torch.matmul(a, L.w2)
+        return layers.rms_norm(f, next_norm, c.norm_eps, residual=h)     # h += f; x = next_norm(h)
+
+    def _qkv(self, L: LayerWeights, x: torch.Tensor, T: int):
+        c = self.config
+        q = torch.matmul(x, L.wq).view(T, c.n_heads, c.head_dim)
+        k = torch.matmul(x, L.wk).view(T, c.n_kv_heads, c.head_dim)
+        v = torch.matmul(x, L.wv).view(T, c.n_kv_heads, c.head_dim)
+        return q, k, v
+
+    # ---------------------------------------------------------------- prefill
+    def prefill(self, tokens: torch.Tensor, positions: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int,
+                slot_mapping: torch.Tensor, kv_cache: KVCache) -> torch.Tensor:
+        """Ragged prefill of several prompts packed along tokens.
+
+        tokens/positions int32 [T]; cu_seqlens int32 [n+1]; slot_mapping int64 [T].
+        Writes every layer's post-RoPE K and raw V into ``kv_cache`` at the slots
+        (fused into the attention kernel) and returns the last-position logits [n, vocab].
+        """
+        c = self.config
+        T = tokens.shape[0]
+        h = layers.embedding(self.tok_embeddings, tokens)
+        x = layers.rms_norm(h, self.layers[0].attention_norm, c.norm_eps)
+        for i, L in enumerate(self.layers):
+            q, k, v = self._qkv(L, x, T)
+            layers.apply_rope_(q, k, self.cos, self.sin, positions)
+            attn = flash_prefill_attention_varlen(q, k, v, cu_seqlens, max_seqlen, True, slot_mapping=slot_mapping,
+                                                  k_cache=kv_cache.k_cache[i], v_cache=kv_cache.v_cache[i])
+            nxt = self.layers[i + 1].attention_norm if i + 1 < c.n_layers else self.norm
+            x = self._layer_ffn(L, h, attn, nxt, T)
+        last = (cu_seqlens[1:] - 1).long()
+        return torch.matmul(x[last], self.output)
+
+    # ----------------------------------------------------------------- decode
+    def decode(self, tokens: torch.Tensor, positions: torch.Tensor, block_tables: torch.Tensor,
+               context_lens: torch.Tensor, slots: torch.Tensor, kv_cache: KVCache,
+               kv_order: str = "reference") -> torch.Tensor:
+        """One decode step for B sequences (llama.py:298-388).
+
+        tokens/positions int32 [B]; block_tables int32 [B, W]; context_lens int32 [B]
+        (= position + 1); slots int64 [B] (the slot of each new token).  Returns
+        logits [B, vocab].
+        """
+        c = self.config
+        B = tokens.shape[0]
+        h = layers.embedding(self.tok_embeddings, tokens)
+        x = layers.rms_norm(h, self.layers[0].attention_norm, c.norm_eps)
+        for i, L in enumerate(self.layers):
+            q, k, v = self._qkv(L, x, B)
+            kc, vc = kv_cache.k_cache[i], kv_cache.v_cache[i]
+            if kv_order == "append_first":
+                layers.apply_rope_write_kv_(q, k, v, self.cos, self.sin, positions, slots, kc, vc)
+            else:
+                layers.apply_rope_(q, k, self.cos, self.sin, positions)
+            attn = paged_decode_attention(q.view(B, 1, c.n_heads, c.head_dim), kc, vc, block_tables, context_lens,
+                                          c.n_heads, c.n_kv_heads, c.head_dim, kv_cache.block_size)
+            if kv_order != "append_first":
+                layers.write_kv_slots(k, v, slots, kc, vc)
+            nxt = self.layers[i + 1].attention_norm if i + 1 < c.n_layers else self.norm
+            x = self._layer_ffn(L, h, attn, nxt, B)
+        return torch.matmul(x, self.output)
