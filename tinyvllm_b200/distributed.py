@@ -1,0 +1,165 @@
+"""Sequence-sharded decoding across the GPUs of one node.
+
+One process per GPU.  Every rank holds the full weights and its own KV pool;
+requests are assigned to ranks as they arrive and never move.  The only data
+exchanged is, once per engine step, an all-gather of the int32 tokens each rank
+sampled (over NCCL on GPUs, or gloo for CPU tests), so that every rank ends the
+step knowing every stream.  The reference models this partitioning in
+``BlockManager(num_gpus, blocks_per_gpu)`` / ``seq_to_gpu``
+(tinyvllm/core/block_manager.py:9-26) but runs one GPU.
+
+Assignment is deterministic and identical on every rank (all ranks see the same
+``add_request`` calls): a new request goes to the rank with the least
+outstanding work, measured as prompt tokens + tokens still to generate, ties to
+the lowest rank -- greedy longest-processing-time balancing of the decode load.
+
+Failure handling: a rank whose local step raises still joins the step's
+collective with an error flag, so every rank raises ``ShardError`` at the same
+step instead of hanging; a rank that dies outright is detected by the process
+group timeout of the next collective.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Any, Dict, List, Optional
+
+import torch
+import torch.distributed as dist
+
+# per-step record layout (int32): [status, has_unfinished, n, (request_id, token, finished) * capacity]
+_HDR = 3
+_OK, _ERROR = 0, 1
+
+
+class ShardError(RuntimeError):
+    """A rank failed during a step; raised on every rank at the same step."""
+
+
+@dataclass
+class _Req:
+    request_id: int
+    rank: int
+    prompt_len: int
+    max_tokens: int
+    tokens: List[int] = field(default_factory=list)
+    finished: bool = False
+
+
+class ShardedEngine:
+    """Drives one local engine per rank and merges the token streams.
+
+    ``engine`` needs ``add_request(prompt, params, request_id=...)``, ``step()``
+    returning finished outputs, ``has_unfinished()``, ``max_batch_size`` and
+    ``num_scheduler_steps``; the new tokens of a step are read from the
+    engine's sequences via ``step_tokens()`` if it has one, else tracked from
+    the running sequences.
+    """
+
+    def __init__(self, engine: Any, rank: int, world_size: int, device: torch.device,
+                 group: Optional[dist.ProcessGroup] = None):
+        self.engine = engine
+        self.rank = rank
+        self.world = world_size
+        self.device = device
+        self.group = group
+        self.requests: Dict[int, _Req] = {}
+        self.next_request_id = 0
+        self.load = [0] * world_size
+        # tokens one rank can emit in one step: a prefill token per admitted sequence
+        # plus one per decode iteration per running sequence
+        self.capacity = engine.max_batch_size * (engine.num_scheduler_steps + 1)
+        self.steps = 0
+
+    # ------------------------------------------------------------------ API
+    def add_request(self, prompt, sampling_params) -> int:
+        rid = self.next_request_id
+        self.next_request_id += 1
+        n_prompt = len(prompt)
+        work = n_prompt + sampling_params.max_tokens
+        rank = min(range(self.world), key=lambda r: (self.load[r], r))
+        self.load[rank] += work
+        self.requests[rid] = _Req(rid, rank, n_prompt, sampling_params.max_tokens)
+        if rank == self.rank:
+            self.engine.add_request(prompt, sampling_params, request_id=rid)
+        return rid
+
+    def owner(self, request_id: int) -> int:
+        return self.requests[request_id].rank
+
+    def has_unfinished(self) -> bool:
+        return any(not r.finished for r in self.requests.values())
+
+    def step(self) -> List[int]:
+        """One engine step on every rank plus the token all-gather.  Returns the ids
+        of requests that finished (on any rank) during this step."""
+        rec = torch.full((_HDR + 3 * self.capacity,), -1, dtype=torch.int32)
+        rec[0] = _OK
+        err: Optional[BaseException] = None
+        try:
+            new = self._local_step()
+            if len(new) > self.capacity:
+                raise RuntimeError(f"{len(new)} tokens in one step exceed the record capacity {self.capacity}")
+            rec[1] = 1 if self.engine.has_unfinished() else 0
+            rec[2] = len(new)
+            for j, (rid, tok, fin) in enumerate(new):
+                rec[_HDR + 3 * j: _HDR + 3 * j + 3] = torch.tensor([rid, tok, int(fin)], dtype=torch.int32)
+        except Exception as e:  # joins the collective anyway, flagged
+            err = e
+            rec[0] = _ERROR
+            rec[1] = 0
+            rec[2] = 0
+        gathered = self._all_gather(rec)
+        self.steps += 1
+        if err is not None:
+            raise ShardError(f"rank {self.rank} failed at step {self.steps}: {err}") from err
+        bad = [r for r in range(self.world) if int(gathered[r, 0]) != _OK]
+        if bad:
+            raise ShardError(f"rank(s) {bad} failed at step {self.steps}")
+        finished = []
+        for r in range(self.world):
+            n = int(gathered[r, 2])
+            for j in range(n):
+                rid, tok, fin = (int(x) for x in gathered[r, _HDR + 3 * j: _HDR + 3 * j + 3])
+                req = self.requests[rid]
+                req.tokens.append(tok)
+                if fin:
+                    req.finished = True
+                    finished.append(rid)
+        return finished
+
+    def run(self) -> Dict[int, List[int]]:
+        while self.has_unfinished():
+            self.step()
+        return {rid: r.tokens for rid, r in self.requests.items()}
+
+    # -------------------------------------------------------------- helpers
+    def _all_gather(self, rec: torch.Tensor) -> torch.Tensor:
+        src = rec.to(self.device)
+        out = torch.empty(self.world * src.numel(), dtype=torch.int32, device=self.device)
+        dist.all_gather_into_tensor(out, src, group=self.group)
+        return out.view(self.world, -1).cpu()
+
+    def _local_step(self):
+        """Run the local engine step; return [(request_id, token, finished)] of the tokens it made."""
+        before = {rid: len(t) for rid, t in self._local_streams().items()}
+        finished_outs = self.engine.step()
+        fin_ids = {o.request_id for o in finished_outs}
+        after = self._local_streams()
+        for o in finished_outs:
+            after[o.request_id] = list(o.tokens)
+        new = []
+        for rid, toks in after.items():
+            k = before.get(rid, 0)
+            for j, t in enumerate(toks[k:]):
+                last = (k + j == len(toks) - 1)
+                new.append((rid, int(t), last and rid in fin_ids))
+        return new
+
+    def _local_streams(self) -> Dict[int, List[int]]:
+        streams = {}
+        for rid, req in getattr(self.engine, "requests", {}).items():
+            seq = getattr(req, "sequence", None)
+            if seq is not None:
+                streams[rid] = list(seq.output_tokens)
+        return streams
