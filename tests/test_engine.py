@@ -61,11 +61,13 @@ def _tiny(dtype, dim, heads, kv_heads, seed=0, max_seq_len=256):
     return Llama(cfg, device="cuda", seed=seed, init_std=0.25)
 
 
+@pytest.mark.parametrize("graphs", [False, True])
 @pytest.mark.parametrize("steps", [1, 3])
-def test_greedy_streams_match_oracle_fp32(cuda, steps):
+def test_greedy_streams_match_oracle_fp32(cuda, steps, graphs):
     model = _tiny("float32", 128, 4, 2)
     prompts, max_toks = _requests(1, 7, 97, 3, 40, 5, 25)
-    got, eng = _run_product(model, prompts, max_toks, max_batch_size=4, num_blocks=24, num_scheduler_steps=steps)
+    got, eng = _run_product(model, prompts, max_toks, max_batch_size=4, num_blocks=24, num_scheduler_steps=steps,
+                            use_cuda_graphs=graphs)
     exp = _run_oracle(model, prompts, max_toks, 4, 24, steps)
     assert got == exp
     assert eng.block_manager.get_num_free_blocks() == 24

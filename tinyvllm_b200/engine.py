@@ -37,6 +37,7 @@ from .block_manager import BlockManager
 from .model import KVCache, Llama
 
 _SAMPLING_EPS = 1e-5
+_GRAPH_BATCHES = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256, 384, 512)
 
 
 @dataclass
@@ -179,7 +180,8 @@ class LLMEngine:
     def __init__(self, model: Llama, tokenizer: Any = None, max_batch_size: int = 8, num_blocks: int = 1024,
                  block_size: int = 16, num_scheduler_steps: int = 1, kv_order: str = "reference",
                  max_table_blocks: Optional[int] = None, gpu_id: int = 0,
-                 output_callback: Optional[Callable[[GenerationOutput], None]] = None):
+                 output_callback: Optional[Callable[[GenerationOutput], None]] = None,
+                 use_cuda_graphs: bool = False):
         if kv_order not in ("reference", "append_first"):
             raise ValueError("kv_order must be 'reference' or 'append_first'")
         self.model = model
@@ -202,6 +204,10 @@ class LLMEngine:
         self.output_callback = output_callback
         self._outputs: List[GenerationOutput] = []
         self.stats = {"prefill_tokens": 0, "decode_tokens": 0, "decode_steps": 0}
+        # decode graphs, one per padded batch size (the reference keeps one TinyJit per batch size)
+        self.use_cuda_graphs = use_cuda_graphs
+        self._graphs = {}
+        self._graph_width = self.table_width or -(-2 * cfg.max_seq_len // block_size)
 
     # ------------------------------------------------------------------ API
     def add_request(self, prompt, sampling_params: Optional[SamplingParams] = None,
@@ -318,16 +324,27 @@ class LLMEngine:
         else:
             slots = new_slots()
             bt = bm.block_table_array(ids, self.table_width)
-        dev = self.device
-        tok = torch.tensor([s.output_tokens[-1] for s in seqs], dtype=torch.int32, device=dev)
-        logits = self.model.decode(tok, torch.from_numpy(pos).to(dev), torch.from_numpy(bt).to(dev),
-                                   torch.from_numpy(ctx).to(dev), torch.from_numpy(slots).to(dev), self.kv_cache,
-                                   self.kv_order)
+        if self.use_cuda_graphs:
+            B = len(seqs)
+            cap = next((b for b in _GRAPH_BATCHES if b >= B), -(-B // 64) * 64)
+            graph = self._graphs.get(cap)
+            if graph is None:
+                graph = self.model.capture_decode(cap, self._graph_width, self.kv_cache, self.kv_order)
+                self._graphs[cap] = graph
+            toks = np.asarray([s.output_tokens[-1] for s in seqs], dtype=np.int32)
+            sampled = graph.run(toks, pos, bt, ctx, slots).tolist()
+        else:
+            dev = self.device
+            tok = torch.tensor([s.output_tokens[-1] for s in seqs], dtype=torch.int32, device=dev)
+            logits = self.model.decode(tok, torch.from_numpy(pos).to(dev), torch.from_numpy(bt).to(dev),
+                                       torch.from_numpy(ctx).to(dev), torch.from_numpy(slots).to(dev),
+                                       self.kv_cache, self.kv_order)
+            sampled = None
         for i in ids:
             bm.advance_position(i)
         self.stats["decode_tokens"] += len(seqs)
         self.stats["decode_steps"] += 1
-        return self._sample(logits, seqs)
+        return sampled if sampled is not None else self._sample(logits, seqs)
 
     def _sample(self, logits: torch.Tensor, seqs: List[Sequence]) -> List[int]:
         """Greedy pick for each row of ``logits`` [len(seqs), vocab] (sampling.py:133-134)."""

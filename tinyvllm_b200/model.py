@@ -204,6 +204,12 @@ class Llama:
         last = (cu_seqlens[1:] - 1).long()
         return torch.matmul(x[last], self.output)
 
+    def capture_decode(self, batch: int, table_width: int, kv_cache: "KVCache",
+                       kv_order: str = "reference") -> "DecodeGraph":
+        """A CUDA graph of one decode step (plus the greedy pick) for ``batch`` rows --
+        the counterpart of the reference's per-batch-size TinyJit (engine.py:157-159)."""
+        return DecodeGraph(self, batch, table_width, kv_cache, kv_order)
+
     # ----------------------------------------------------------------- decode
     def decode(self, tokens: torch.Tensor, positions: torch.Tensor, block_tables: torch.Tensor,
                context_lens: torch.Tensor, slots: torch.Tensor, kv_cache: KVCache,
@@ -232,3 +238,68 @@ class Llama:
             nxt = self.layers[i + 1].attention_norm if i + 1 < c.n_layers else self.norm
             x = self._layer_ffn(L, h, attn, nxt, B)
         return torch.matmul(x, self.output)
+
+
+class DecodeGraph:
+    """One decode step of ``Llama.decode`` followed by the greedy argmax, captured as a
+    CUDA graph over static input buffers.  ``run`` copies a step's inputs from host
+    arrays into the buffers, replays the graph and returns the sampled tokens.
+
+    Rows beyond the live batch are padding: token 0, context 1 over block 0,
+    slot -1 (no K/V write), and their outputs are ignored.
+    """
+
+    def __init__(self, model: Llama, batch: int, table_width: int, kv_cache: KVCache, kv_order: str):
+        dev = model.device
+        self.model, self.batch, self.width, self.kv_cache, self.kv_order = model, batch, table_width, kv_cache, kv_order
+        self.tok = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.bt = torch.zeros(batch, table_width, dtype=torch.int32, device=dev)
+        self.ctx = torch.ones(batch, dtype=torch.int32, device=dev)
+        self.slots = torch.full((batch,), -1, dtype=torch.int64, device=dev)
+        self.out = torch.zeros(batch, dtype=torch.int32, device=dev)
+        # pinned staging for the per-step host -> device copies
+        self.h_tok = torch.zeros(batch, dtype=torch.int32).pin_memory()
+        self.h_pos = torch.zeros(batch, dtype=torch.int32).pin_memory()
+        self.h_bt = torch.zeros(batch, table_width, dtype=torch.int32).pin_memory()
+        self.h_ctx = torch.ones(batch, dtype=torch.int32).pin_memory()
+        self.h_slots = torch.full((batch,), -1, dtype=torch.int64).pin_memory()
+        self.h_out = torch.zeros(batch, dtype=torch.int32).pin_memory()
+        self.stream = torch.cuda.Stream(dev)
+        self.stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(self.stream):
+            for _ in range(2):   # warm-up: workspaces, kernel attributes, cuBLAS handles
+                self._forward()
+        self.stream.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self._forward()
+        self.stream.synchronize()
+
+    def _forward(self):
+        logits = self.model.decode(self.tok, self.pos, self.bt, self.ctx, self.slots, self.kv_cache, self.kv_order)
+        layers.greedy_argmax(logits, out=self.out)
+
+    def run(self, tokens: np.ndarray, positions: np.ndarray, tables: np.ndarray, ctx: np.ndarray,
+            slots: np.ndarray) -> np.ndarray:
+        n = tokens.shape[0]
+        if n > self.batch or tables.shape[1] > self.width:
+            raise ValueError("step larger than the captured graph")
+        ht, hp, hb, hc, hs = (x.numpy() for x in (self.h_tok, self.h_pos, self.h_bt, self.h_ctx, self.h_slots))
+        ht[:n], hp[:n], hc[:n], hs[:n] = tokens, positions, ctx, slots
+        ht[n:], hp[n:], hc[n:], hs[n:] = 0, 0, 1, -1
+        hb[:] = 0
+        hb[:n, :tables.shape[1]] = tables
+        cur = torch.cuda.current_stream(self.model.device)
+        self.stream.wait_stream(cur)
+        with torch.cuda.stream(self.stream):
+            self.tok.copy_(self.h_tok, non_blocking=True)
+            self.pos.copy_(self.h_pos, non_blocking=True)
+            self.bt.copy_(self.h_bt, non_blocking=True)
+            self.ctx.copy_(self.h_ctx, non_blocking=True)
+            self.slots.copy_(self.h_slots, non_blocking=True)
+            self.graph.replay()
+            self.h_out.copy_(self.out, non_blocking=True)
+        self.stream.synchronize()
+        cur.wait_stream(self.stream)
+        return self.h_out.numpy()[:n].copy()
