@@ -447,6 +447,122 @@ def run_e2e(args, rank: int, world: int, local_rank: int) -> int:
     return 0
 
 
+def run_e2e8b(args, rank: int, world: int, local_rank: int) -> int:
+    """Config 5: random-init Llama-3-8B-shaped model in bf16; 512 sequences with
+    contexts ~ U{512..8192} whose K/V is synthetic N(0,1) already in the pool,
+    256 greedy tokens each, sharded by sequence over the ranks (least outstanding
+    work first) with one int32 token all-gather per step over NCCL.  Each rank
+    keeps resident as many of its sequences as its HBM holds (weights are
+    replicated).  A step is one engine step (one decode iteration for every
+    resident sequence on every rank); value = tokens produced by all ranks / s."""
+    import datetime
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from tinyvllm_b200.distributed import ShardedEngine
+    from tinyvllm_b200.engine import LLMEngine, SamplingParams
+    from tinyvllm_b200.model import Llama, llama3_8b_config
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    else:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29533")
+        dist.init_process_group("nccl", device_id=dev, rank=0, world_size=1,
+                                timeout=datetime.timedelta(seconds=300))
+    cfg = llama3_8b_config("bfloat16")
+    model = Llama(cfg, device=dev, seed=1234 + 5)
+    n_total, gen = 512, 256
+    rng = np.random.default_rng(1239)
+    ctx = rng.integers(512, 8193, size=n_total)
+    first = rng.integers(0, cfg.vocab_size, size=n_total)
+    prompts = [rng.integers(0, cfg.vocab_size, size=int(c)).tolist() for c in ctx]
+    # replay the sharding (same rule as ShardedEngine) to size this rank's pool
+    loads = [0] * world
+    mine = []
+    for i, c in enumerate(ctx):
+        r = min(range(world), key=lambda x: (loads[x], x))
+        loads[r] += int(c) + gen
+        if r == rank:
+            mine.append(i)
+    steps_total = args.warmup + args.steps + 2
+    tok_bytes = cfg.n_layers * cfg.n_kv_heads * cfg.head_dim * 2 * 2
+    free, _ = torch.cuda.mem_get_info(dev)
+    budget = free - (8 << 30)                     # activations, graphs, workspaces
+    resident, blocks = 0, 0
+    for i in mine:
+        b = -(-(int(ctx[i]) + steps_total) // 16)
+        if (blocks + b) * 16 * tok_bytes > budget:
+            break
+        resident += 1
+        blocks += b
+    width = -(-(int(ctx.max()) + steps_total) // 16)
+    eng = LLMEngine(model, max_batch_size=resident, num_blocks=blocks + 8, num_scheduler_steps=1,
+                    kv_order="reference", max_table_blocks=width, use_cuda_graphs=True)
+    for t in eng.kv_cache.k_cache + eng.kv_cache.v_cache:
+        t.normal_()                                # synthetic pre-filled K/V
+    sharded = ShardedEngine(eng, rank, world, dev)
+    for i in range(n_total):
+        sharded.add_request(prompts[i], SamplingParams(max_tokens=gen), prefilled_first_token=int(first[i]))
+    for _ in range(args.warmup):
+        sharded.step()
+    torch.cuda.synchronize(dev)
+    dist.barrier(device_ids=[local_rank])
+    clocks = ClockSampler(world) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    dist.barrier(device_ids=[local_rank])
+    n0 = sum(len(r.tokens) for r in sharded.requests.values())
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    ev0.record()
+    for _ in range(args.steps):
+        sharded.step()
+    ev1.record()
+    torch.cuda.synchronize(dev)
+    wall = time.perf_counter() - t0
+    dist.barrier(device_ids=[local_rank])
+    clk = clocks.stop() if clocks else None
+    made = sum(len(r.tokens) for r in sharded.requests.values()) - n0
+    running = [s for s in eng.scheduler.running.values()]
+    ctx_sum = sum(s.get_len() for s in running)
+    stats = torch.tensor([wall, ev0.elapsed_time(ev1) / 1e3, resident, ctx_sum], dtype=torch.float64, device=dev)
+    allst = torch.empty(world * 4, dtype=torch.float64, device=dev)
+    dist.all_gather_into_tensor(allst, stats)
+    allst = allst.view(world, 4).cpu().numpy()
+    del eng._graphs
+    if rank == 0:
+        secs = float(allst[:, 0].max())
+        step_s = secs / args.steps
+        w_bytes = sum(p.numel() * p.element_size() for L in model.layers for p in
+                      (L.wq, L.wk, L.wv, L.wo, L.w13, L.w2)) + model.output.numel() * 2
+        kv_bytes = float(allst[0, 3]) * tok_bytes
+        hbm, kind = _peaks()
+        achieved = (w_bytes + kv_bytes) / step_s / 1e9
+        line = {
+            "metric": "e2e decode tok/s (config 5: Llama-3-8B shape bf16, 512 seqs ctx U[512,8192], "
+                      "sequence-sharded)",
+            "value": made / secs, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (random-init weights, synthetic N(0,1) pre-filled K/V)",
+            "config": {"workload": "config5 sharded decode", "sequences": n_total,
+                       "resident_per_rank": [int(x) for x in allst[:, 2]],
+                       "ctx_sum_per_rank": [int(x) for x in allst[:, 3]],
+                       "parallelism": f"sequence-sharded x{world}, int32 token all-gather per step (NCCL)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "peak_kind": kind,
+                         "note": "rank 0: (weights + live K/V bytes per step) / step time"},
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier(device_ids=[local_rank])
+    dist.destroy_process_group()
+    return 0
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -456,9 +572,9 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=256,
                     help="sequences per GPU (default 256 = config 3; smaller only for profiling captures)")
-    ap.add_argument("--workload", choices=["decode", "prefill", "e2e"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "e2e", "e2e8b"], default="decode",
                     help="decode = config 3 paged decode (the headline); prefill = config 2 flash prefill; "
-                         "e2e = config 4 TinyLlama engine")
+                         "e2e = config 4 TinyLlama engine; e2e8b = config 5 sharded Llama-3-8B-shape decode")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -471,6 +587,8 @@ def main() -> int:
         return run_prefill(args, rank, world, local_rank)
     if args.workload == "e2e":
         return run_e2e(args, rank, world, local_rank)
+    if args.workload == "e2e8b":
+        return run_e2e8b(args, rank, world, local_rank)
     return run_ours(args, rank, world, local_rank)
 
 

@@ -24,6 +24,7 @@ from __future__ import annotations
 from dataclasses import dataclass, field
 from typing import Any, Dict, List, Optional
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -52,8 +53,8 @@ class ShardedEngine:
     ``engine`` needs ``add_request(prompt, params, request_id=...)``, ``step()``
     returning finished outputs, ``has_unfinished()``, ``max_batch_size`` and
     ``num_scheduler_steps``; the new tokens of a step are read from the
-    engine's sequences via ``step_tokens()`` if it has one, else tracked from
-    the running sequences.
+    engine's request table (``engine.requests[rid].sequence.output_tokens``)
+    and its finished outputs.
     """
 
     def __init__(self, engine: Any, rank: int, world_size: int, device: torch.device,
@@ -72,7 +73,9 @@ class ShardedEngine:
         self.steps = 0
 
     # ------------------------------------------------------------------ API
-    def add_request(self, prompt, sampling_params) -> int:
+    def add_request(self, prompt, sampling_params, prefilled_first_token: Optional[int] = None) -> int:
+        """Assign a request to a rank (least outstanding work) and hand it to that rank's
+        engine; with ``prefilled_first_token`` the owner admits it as already prefilled."""
         rid = self.next_request_id
         self.next_request_id += 1
         n_prompt = len(prompt)
@@ -81,7 +84,10 @@ class ShardedEngine:
         self.load[rank] += work
         self.requests[rid] = _Req(rid, rank, n_prompt, sampling_params.max_tokens)
         if rank == self.rank:
-            self.engine.add_request(prompt, sampling_params, request_id=rid)
+            if prefilled_first_token is None:
+                self.engine.add_request(prompt, sampling_params, request_id=rid)
+            else:
+                self.engine.add_prefilled_request(prompt, sampling_params, prefilled_first_token, request_id=rid)
         return rid
 
     def owner(self, request_id: int) -> int:
@@ -93,7 +99,7 @@ class ShardedEngine:
     def step(self) -> List[int]:
         """One engine step on every rank plus the token all-gather.  Returns the ids
         of requests that finished (on any rank) during this step."""
-        rec = torch.full((_HDR + 3 * self.capacity,), -1, dtype=torch.int32)
+        rec = np.full(_HDR + 3 * self.capacity, -1, dtype=np.int32)
         rec[0] = _OK
         err: Optional[BaseException] = None
         try:
@@ -102,14 +108,14 @@ class ShardedEngine:
                 raise RuntimeError(f"{len(new)} tokens in one step exceed the record capacity {self.capacity}")
             rec[1] = 1 if self.engine.has_unfinished() else 0
             rec[2] = len(new)
-            for j, (rid, tok, fin) in enumerate(new):
-                rec[_HDR + 3 * j: _HDR + 3 * j + 3] = torch.tensor([rid, tok, int(fin)], dtype=torch.int32)
+            if new:
+                rec[_HDR:_HDR + 3 * len(new)] = np.asarray(new, dtype=np.int32).reshape(-1)
         except Exception as e:  # joins the collective anyway, flagged
             err = e
             rec[0] = _ERROR
             rec[1] = 0
             rec[2] = 0
-        gathered = self._all_gather(rec)
+        gathered = self._all_gather(torch.from_numpy(rec))
         self.steps += 1
         if err is not None:
             raise ShardError(f"rank {self.rank} failed at step {self.steps}: {err}") from err
@@ -119,8 +125,8 @@ class ShardedEngine:
         finished = []
         for r in range(self.world):
             n = int(gathered[r, 2])
-            for j in range(n):
-                rid, tok, fin = (int(x) for x in gathered[r, _HDR + 3 * j: _HDR + 3 * j + 3])
+            rows = gathered[r, _HDR:_HDR + 3 * n].reshape(n, 3)
+            for rid, tok, fin in rows.tolist():
                 req = self.requests[rid]
                 req.tokens.append(tok)
                 if fin:
@@ -134,32 +140,24 @@ class ShardedEngine:
         return {rid: r.tokens for rid, r in self.requests.items()}
 
     # -------------------------------------------------------------- helpers
-    def _all_gather(self, rec: torch.Tensor) -> torch.Tensor:
+    def _all_gather(self, rec: torch.Tensor) -> np.ndarray:
         src = rec.to(self.device)
         out = torch.empty(self.world * src.numel(), dtype=torch.int32, device=self.device)
         dist.all_gather_into_tensor(out, src, group=self.group)
-        return out.view(self.world, -1).cpu()
+        return out.view(self.world, -1).cpu().numpy()
 
     def _local_step(self):
         """Run the local engine step; return [(request_id, token, finished)] of the tokens it made."""
-        before = {rid: len(t) for rid, t in self._local_streams().items()}
+        reqs = getattr(self.engine, "requests", {})
+        before = {rid: len(r.sequence.output_tokens) for rid, r in reqs.items()
+                  if getattr(r, "sequence", None) is not None}
         finished_outs = self.engine.step()
-        fin_ids = {o.request_id for o in finished_outs}
-        after = self._local_streams()
-        for o in finished_outs:
-            after[o.request_id] = list(o.tokens)
         new = []
-        for rid, toks in after.items():
-            k = before.get(rid, 0)
-            for j, t in enumerate(toks[k:]):
-                last = (k + j == len(toks) - 1)
-                new.append((rid, int(t), last and rid in fin_ids))
-        return new
-
-    def _local_streams(self) -> Dict[int, List[int]]:
-        streams = {}
-        for rid, req in getattr(self.engine, "requests", {}).items():
-            seq = getattr(req, "sequence", None)
+        for rid, r in reqs.items():                 # still running after the step
+            seq = getattr(r, "sequence", None)
             if seq is not None:
-                streams[rid] = list(seq.output_tokens)
-        return streams
+                new.extend((rid, int(t), 0) for t in seq.output_tokens[before.get(rid, 0):])
+        for o in finished_outs:
+            tail = list(o.tokens)[before.get(o.request_id, 0):]
+            new.extend((o.request_id, int(t), int(j == len(tail) - 1)) for j, t in enumerate(tail))
+        return new

@@ -91,6 +91,7 @@ class Request:
     sampling_params: SamplingParams
     arrival_time: float = field(default_factory=time.time)
     sequence: Optional[Sequence] = None
+    prefilled_first_token: Optional[int] = None
 
 
 @dataclass
@@ -230,6 +231,16 @@ class LLMEngine:
         self.scheduler.add_request(req)
         return request_id
 
+    def add_prefilled_request(self, context_tokens, sampling_params: Optional[SamplingParams] = None,
+                              first_token: int = 0, request_id: Optional[int] = None) -> int:
+        """Admit a sequence whose K/V for ``context_tokens`` is already resident in the
+        pool contents (e.g. synthetic K/V for a decode benchmark): on admission its
+        blocks are allocated and its position advanced as a prefill would, no
+        prefill is run, and ``first_token`` is taken as the prompt's sampled token."""
+        rid = self.add_request(context_tokens, sampling_params, request_id)
+        self.requests[rid].prefilled_first_token = int(first_token)
+        return rid
+
     def has_unfinished(self) -> bool:
         return self.scheduler.has_unfinished()
 
@@ -289,6 +300,23 @@ class LLMEngine:
 
     # --------------------------------------------------------------- device
     def _prefill(self, seqs: List[Sequence]) -> List[int]:
+        bm = self.block_manager
+        first = {}
+        live = []
+        for s in seqs:
+            tok = self.requests[s.request_id].prefilled_first_token
+            if tok is None:
+                live.append(s)
+            else:                      # K/V already resident: allocate and advance only
+                bm.slot_mapping(s.seq_id, 0, s.get_prompt_len())
+                bm.advance_position(s.seq_id, s.get_prompt_len())
+                first[s.seq_id] = tok
+        if live:
+            for s, t in zip(live, self._prefill_live(live)):
+                first[s.seq_id] = t
+        return [first[s.seq_id] for s in seqs]
+
+    def _prefill_live(self, seqs: List[Sequence]) -> List[int]:
         bm = self.block_manager
         lens = [s.get_prompt_len() for s in seqs]
         slots = np.concatenate([bm.slot_mapping(s.seq_id, 0, L) for s, L in zip(seqs, lens)])
