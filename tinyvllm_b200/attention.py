@@ -17,14 +17,14 @@ import torch
 from . import _lib
 
 _ws_lock = threading.Lock()
-_workspaces: Dict[Tuple[int, int], torch.Tensor] = {}
+_workspaces: Dict[Tuple[int, int, str], torch.Tensor] = {}
 
 
-def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """Per-(device, stream) scratch buffer, grown on demand, zeroed when created
-    (its first word is the kernels' time-out status)."""
+def _workspace(device: torch.device, nbytes: int, kind: str = "decode") -> torch.Tensor:
+    """Per-(device, stream, kernel family) scratch buffer, grown on demand and zeroed
+    when created (its first word is the kernels' time-out status)."""
     key = (device.index if device.index is not None else torch.cuda.current_device(),
-           torch.cuda.current_stream(device).cuda_stream)
+           torch.cuda.current_stream(device).cuda_stream, kind)
     with _ws_lock:
         ws = _workspaces.get(key)
         if ws is None or ws.numel() < nbytes:
@@ -33,10 +33,10 @@ def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
         return ws
 
 
-def workspace_status(device: Optional[torch.device] = None) -> int:
+def workspace_status(device: Optional[torch.device] = None, kind: str = "decode") -> int:
     """Status word of the current stream's workspace (non-zero: a kernel wait timed out)."""
     device = device or torch.device("cuda", torch.cuda.current_device())
-    ws = _workspace(device, 0)
+    ws = _workspace(device, 0, kind)
     return int(ws[:4].view(torch.int32).item())
 
 
@@ -130,7 +130,7 @@ def flash_prefill_attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Te
     if out is None:
         out = torch.empty_like(q)
     L = _lib.lib()
-    ws = _workspace(dev, L.tvk_flash_prefill_workspace_size(n_seqs, T))
+    ws = _workspace(dev, L.tvk_flash_prefill_workspace_size(n_seqs, T), "prefill")
     rc = L.tvk_flash_prefill_attention(
         _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(out), _lib.ptr(cu_seqlens), n_seqs, int(max_seqlen), T,
         Hq, Hkv, D, 1 if causal else 0, _lib.dtype_code(q), _lib.ptr(slot_mapping), _lib.ptr(k_cache),
