@@ -214,15 +214,16 @@ int tvk_paged_decode_attention_noalloc(const void* q, const void* k_cache, const
 
 /*
  * Tensor-core layout self-test (no reference counterpart): one 128 x n x k
- * tcgen05 GEMM through the operand paths the prefill kernel uses (thread-
- * written swizzled A, TMA-loaded B, TMEM accumulator).
+ * tcgen05 GEMM through the operand paths the prefill kernel uses (A written
+ * swizzled into shared memory by threads, or into TMEM with tcgen05.st when
+ * a_in_tmem != 0; TMA-loaded B; TMEM accumulator).
  *   b_mn_major == 0: c[128,n] = a[128,k] . b[n,k]^T
  *   b_mn_major == 1: c[128,n] = a[128,k] . b[k,n]
  * n, k in {64, 128}; dtype TVK_DTYPE_F16 or TVK_DTYPE_BF16; c is fp32.
  * `status` (device int, may be NULL) is set to 1 if a bounded wait expired.
  */
 int tvk_selftest_umma_gemm(const void* a, const void* b, float* c, int n, int k, int b_mn_major,
-                           int dtype, int* status, void* stream);
+                           int a_in_tmem, int dtype, int* status, void* stream);
 
 #ifdef __cplusplus
 }

@@ -29,7 +29,7 @@ SIGNATURES = {
         _c_int,
         [_c_void] * 6 + [_c_int] * 9 + [_c_void, _c_size, _c_void],
     ),
-    "tvk_selftest_umma_gemm": (_c_int, [_c_void] * 3 + [_c_int] * 4 + [_c_void, _c_void]),
+    "tvk_selftest_umma_gemm": (_c_int, [_c_void] * 3 + [_c_int] * 5 + [_c_void, _c_void]),
     "tvk_paged_decode_attention_noalloc": (_c_int, [_c_void] * 6 + [_c_int] * 9 + [_c_void]),
     "tvk_rms_norm": (_c_int, [_c_void] * 5 + [_c_int, _c_int, _c_float, _c_int, _c_void]),
     "tvk_rope": (_c_int, [_c_void] * 5 + [_c_int] * 6 + [_c_void]),

@@ -14,7 +14,7 @@ namespace {
 template <typename T>
 __global__ void __launch_bounds__(128, 1)
     umma_selftest_kernel(const T* __restrict__ a, float* __restrict__ c, int n, int k, int b_mn_major,
-                         int* status, const __grid_constant__ CUtensorMap tm_b) {
+                         int a_in_tmem, int* status, const __grid_constant__ CUtensorMap tm_b) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = ptx::smem_u32(smem_raw);
   const uint32_t base_u32 = (raw + 1023u) & ~1023u;
@@ -27,7 +27,7 @@ __global__ void __launch_bounds__(128, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5;
   if (warp == 0) {
-    umma::tmem_alloc(tmem_slot, 128);
+    umma::tmem_alloc(tmem_slot, 256);  // D in columns [0, n), A (when in TMEM) in [128, 128 + k/2)
     umma::tmem_relinquish();
   }
   if (tid == 0) {
@@ -46,6 +46,20 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
+  if (a_in_tmem) {
+    // row r of A -> TMEM lane r, columns 128 + j hold elements (2j, 2j+1)
+    const int row = warp * 32 + (tid & 31);
+    for (int c0 = 0; c0 < k / 2; c0 += 32) {
+      uint32_t u[32];
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(a + (size_t)row * k) + c0;
+      for (int j = 0; j < 32; ++j) u[j] = src[j];
+      umma::st_32x32b_x32_u(tmem + ((uint32_t)(warp * 32) << 16) + 128 + c0, u);
+    }
+    umma::st_wait();
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
 
   bool ok = true;
   if (tid == 0) {
@@ -80,7 +94,10 @@ __global__ void __launch_bounds__(128, 1)
           bd = umma::smem_desc_sw128(ptx::smem_u32(sb) + (ks / 4) * n * 128 + (ks % 4) * 32, 16, 1024);
         else
           bd = umma::smem_desc_sw128(ptx::smem_u32(sb) + ks * 16 * 128, k * 128, 1024);
-        umma::mma_f16_ss(tmem, ad, bd, idesc, ks > 0 ? 1u : 0u);
+        if (a_in_tmem)
+          umma::mma_f16_ts(tmem, tmem + 128 + ks * 8, bd, idesc, ks > 0 ? 1u : 0u);
+        else
+          umma::mma_f16_ss(tmem, ad, bd, idesc, ks > 0 ? 1u : 0u);
       }
       umma::commit(bar_mma);
     }
@@ -103,17 +120,19 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   if (warp == 0) {
     umma::fence_after_sync();
-    umma::tmem_dealloc(tmem, 128);
+    umma::tmem_dealloc(tmem, 256);
   }
 }
 
 }  // namespace
 
+// A comes from shared memory (written swizzled by threads) or, with a_in_tmem,
+// from TMEM (written with tcgen05.st, two elements per column).
 // C[128, n] (fp32) = A[128, k] . B^T  (B given [n, k]) when b_mn_major == 0,
 //                  = A[128, k] . B    (B given [k, n]) when b_mn_major == 1.
 // n, k in {64, 128}; dtype fp16 or bf16.  status (may be null) gets 1 on a wait time-out.
 extern "C" int tvk_selftest_umma_gemm(const void* a, const void* b, float* c, int n, int k, int b_mn_major,
-                                      int dtype, int* status, void* stream) {
+                                      int a_in_tmem, int dtype, int* status, void* stream) {
   TVK_CHECK_ARG(a && b && c, "null pointer argument");
   TVK_CHECK_ARG((n == 64 || n == 128) && (k == 64 || k == 128), "n and k must be 64 or 128");
   TVK_CHECK_ARG(dtype == TVK_DTYPE_F16 || dtype == TVK_DTYPE_BF16, "dtype must be fp16 or bf16");
@@ -140,12 +159,13 @@ extern "C" int tvk_selftest_umma_gemm(const void* a, const void* b, float* c, in
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == TVK_DTYPE_F16) {
     TVK_CHECK_CUDA(cudaFuncSetAttribute(umma_selftest_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    umma_selftest_kernel<__half><<<1, 128, smem, s>>>(static_cast<const __half*>(a), c, n, k, b_mn_major, status, tm);
+    umma_selftest_kernel<__half><<<1, 128, smem, s>>>(static_cast<const __half*>(a), c, n, k, b_mn_major, a_in_tmem,
+                                                     status, tm);
   } else {
     TVK_CHECK_CUDA(
         cudaFuncSetAttribute(umma_selftest_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     umma_selftest_kernel<__nv_bfloat16><<<1, 128, smem, s>>>(static_cast<const __nv_bfloat16*>(a), c, n, k,
-                                                             b_mn_major, status, tm);
+                                                             b_mn_major, a_in_tmem, status, tm);
   }
   TVK_CHECK_LAUNCH("umma_selftest");
   return TVK_OK;
