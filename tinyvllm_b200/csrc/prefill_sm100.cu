@@ -85,14 +85,12 @@ struct PfCfg {
   static constexpr int kKB = D / 64;               // 64-element (128 B) column blocks per row
   static constexpr int kBlockBytes = 128 * 128;    // one column block of a 128-row tile
   static constexpr int kTileBytes = 128 * D * 2;   // one 128-row tile of Q, K or V
-  static constexpr int kStages = 2;                // K/V ring depth
+  static constexpr int kStages = 3;                // K/V ring depth
   static constexpr int kSBufs = D == 64 ? 1 : 2;   // S buffers in TMEM
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kQOff + kTileBytes;
   static constexpr int kVOff = kKOff + kStages * kTileBytes;
-  static constexpr int kPOff = kVOff + kStages * kTileBytes;
-  static constexpr int kPBytes = 128 * 128 * 2;    // P tile: 128 rows x 128 keys
-  static constexpr int kBarOff = kPOff + kPBytes;
+  static constexpr int kBarOff = kVOff + kStages * kTileBytes;
   // q_full, q_empty, k_full[S], v_full[S], kv_empty[S], s_full[SB], s_empty[SB], p_full, pv_done, o_empty, final
   static constexpr int kNumBars = 2 + 3 * kStages + 2 * kSBufs + 4;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag
@@ -101,8 +99,11 @@ struct PfCfg {
   // the slack above kUsed absorbs the 1024-byte alignment of the base.
   static constexpr int kCtasPerSm = D == 64 ? 2 : 1;
   static constexpr int kSmemBytes = D == 64 ? 115712 : kUsed + 1024;
-  static constexpr uint32_t kTmemCols = D == 64 ? 256 : 512;
-  static constexpr uint32_t kOCol = kSBufs * 128;  // O accumulator after the S buffers
+  // TMEM columns: S buffers, then the O accumulator, then P (128 keys as 64
+  // columns of packed 16-bit pairs, the A operand of P.V)
+  static constexpr uint32_t kOCol = kSBufs * 128;
+  static constexpr uint32_t kPCol = kOCol + D;
+  static constexpr uint32_t kTmemCols = kPCol + 64 <= 256 ? 256 : 512;
   static_assert(kUsed <= kSmemBytes, "shared memory layout overflows");
 };
 
@@ -276,13 +277,11 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
           if (i == 0 && !wait_or_abort(o_empty, (item_it & 1) ^ 1, abort_flag)) return false;
           if (!wait_or_abort(&v_full[st], (g / S) & 1, abort_flag)) return false;
           umma::fence_after_sync();
-          const uint32_t p_addr = base_u32 + C::kPOff;
           const uint32_t v_addr = base_u32 + C::kVOff + st * C::kTileBytes;
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
-            const uint64_t ad = umma::smem_desc_sw128(p_addr + (ks >> 2) * C::kBlockBytes + (ks & 3) * 32, 16, 1024);
+          for (int ks = 0; ks < 8; ++ks) {  // 16 keys per MMA: 8 TMEM columns of P
             const uint64_t bd = umma::smem_desc_sw128(v_addr + ks * 2048, C::kBlockBytes, 1024);
-            umma::mma_f16_ss(tmem + C::kOCol, ad, bd, idesc_o, (i > 0 || ks > 0) ? 1u : 0u);
+            umma::mma_f16_ts(tmem + C::kOCol, tmem + C::kPCol + ks * 8, bd, idesc_o, (i > 0 || ks > 0) ? 1u : 0u);
           }
           umma::commit(pv_done);
           umma::commit(&kv_empty[st]);
@@ -331,7 +330,6 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
     bool ok = true;
     int k = 0;
     Item it;
-    uint8_t* prow = base + C::kPOff;
     while (ok && next_item(p, n_items, k, it)) {
       const int n_kv = p.causal ? it.mtile + 1 : (it.L + 127) / 128;
       const int q_pos = it.mtile * 128 + r;
@@ -389,9 +387,15 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
           l *= corr;
           m = m_cand;
         }
-        // pass 2: P = 2^(s*scale - m) packed to fp16/bf16 in registers (64 columns per load)
+        // P (TMEM, single-buffered) is still the A operand of the previous P.V until it completes
+        if (!pv_waited) {
+          ok = __all_sync(0xffffffffu, wait_or_abort(pv_done, pv_it & 1, abort_flag));
+          if (!ok) break;
+          ++pv_it;
+        }
+        // pass 2: P = 2^(s*scale - m), packed to fp16/bf16 pairs and stored to TMEM
+        // (row r = lane, 64 columns for 128 keys): the A operand of P.V
         float sum = 0.f;
-        uint32_t pk[64];
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
           float s[64];
@@ -402,34 +406,24 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
 #pragma unroll
             for (int x = 0; x < 64; ++x) s[x] = hf * 64 + x < lim_rel ? s[x] : -INFINITY;
           }
+          uint32_t pk[32];
 #pragma unroll
           for (int x = 0; x < 32; ++x) {
             const float p0 = ex2(fmaf(s[2 * x], sl2, -m));
             const float p1 = ex2(fmaf(s[2 * x + 1], sl2, -m));
             sum += p0 + p1;
-            pk[hf * 32 + x] = DT<T>::pack2(p0, p1);
+            pk[x] = DT<T>::pack2(p0, p1);
           }
+          umma::st_32x32b_x32_u(t_lane + C::kPCol + hf * 32, pk);
         }
+        umma::st_wait();
         // S has been read: hand the TMEM buffer back to the MMA warp.
         umma::fence_before_sync();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&s_empty[sb]);
         ++s_it;
-        if (!pv_waited) {
-          ok = __all_sync(0xffffffffu, wait_or_abort(pv_done, pv_it & 1, abort_flag));
-          if (!ok) break;
-          ++pv_it;
-        }
-        // P -> shared memory, swizzled K-major rows of 128 keys
-#pragma unroll
-        for (int c8 = 0; c8 < 16; ++c8) {
-          const int kb = c8 >> 3;
-          const uint32_t off = kb * C::kBlockBytes + r * 128 + ((((c8 & 7) ^ (r & 7)) & 7) << 4);
-          *reinterpret_cast<uint4*>(prow + off) = make_uint4(pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
-        }
         l += sum;
         umma::fence_before_sync();
-        umma::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(p_full);
       }
