@@ -538,7 +538,7 @@ def run_e2e8b(args, rank: int, world: int, local_rank: int) -> int:
         secs = float(allst[:, 0].max())
         step_s = secs / args.steps
         w_bytes = sum(p.numel() * p.element_size() for L in model.layers for p in
-                      (L.wq, L.wk, L.wv, L.wo, L.w13, L.w2)) + model.output.numel() * 2
+                      (L.wqkv, L.wo, L.w13, L.w2)) + model.output.numel() * 2
         kv_bytes = float(allst[0, 3]) * tok_bytes
         hbm, kind = _peaks()
         achieved = (w_bytes + kv_bytes) / step_s / 1e9

@@ -152,6 +152,21 @@ int tvk_rope_write_kv(void* q, void* k, const void* v, const float* cos_table, c
                       int num_blocks, int block_size, int dtype, void* stream);
 
 /*
+ * Split one packed projection row per token, qkv[t] = [q (n_heads*head_dim) |
+ * k (n_kv_heads*head_dim) | v (n_kv_heads*head_dim)] with row stride `row_stride`
+ * elements (the output of one GEMM against the concatenated wq|wk|wv,
+ * llama.py:174-176), into contiguous q [n_tokens, n_heads, head_dim] and k, v
+ * [n_tokens, n_kv_heads, head_dim], applying RoPE to q and k as tvk_rope does
+ * (llama.py:178-179).  With slots != NULL the roped k and the v rows are also
+ * stored at their paged slots like tvk_rope_write_kv (k_cache/v_cache and the
+ * pool sizes are ignored otherwise).
+ */
+int tvk_qkv_rope(const void* qkv, long long row_stride, void* q, void* k, void* v, const float* cos_table,
+                 const float* sin_table, const int32_t* positions, const int64_t* slots, void* k_cache,
+                 void* v_cache, int n_tokens, int n_heads, int n_kv_heads, int head_dim, int max_pos,
+                 int num_blocks, int block_size, int dtype, void* stream);
+
+/*
  * k/v rows [n_tokens, n_kv_heads, head_dim] -> paged slots, KVCache.write_kv
  * (core/kv_cache.py:34-38); one launch for a whole decode batch replaces the
  * reference's per-sequence, per-layer writes (llama.py:381-386).

@@ -53,12 +53,12 @@ def _run_oracle(model, prompts, max_toks, max_batch_size, num_blocks, num_schedu
     return (eng.outputs, eng.gaps) if with_gaps else eng.outputs
 
 
-def _tiny(dtype, dim, heads, kv_heads, seed=0, max_seq_len=256):
+def _tiny(dtype, dim, heads, kv_heads, seed=0, max_seq_len=256, init_std=0.25):
     from tinyvllm_b200.model import Llama, LlamaConfig
     cfg = LlamaConfig(dim=dim, n_layers=2, n_heads=heads, n_kv_heads=kv_heads, vocab_size=97, hidden_dim=2 * dim,
                       max_seq_len=max_seq_len, dtype=dtype)
-    # std 0.25 keeps the logits spread wide enough that float rounding cannot flip the argmax
-    return Llama(cfg, device="cuda", seed=seed, init_std=0.25)
+    # std 0.25 keeps the logits spread wide enough that fp32 rounding cannot flip the argmax
+    return Llama(cfg, device="cuda", seed=seed, init_std=init_std)
 
 
 @pytest.mark.parametrize("graphs", [False, True])
@@ -73,18 +73,19 @@ def test_greedy_streams_match_oracle_fp32(cuda, steps, graphs):
     assert eng.block_manager.get_num_free_blocks() == 24
 
 
-@pytest.mark.parametrize("dtype,tol", [("float16", 0.5), ("bfloat16", 1.5)])
-def test_half_precision_engine_tracks_oracle(cuda, dtype, tol):
+@pytest.mark.parametrize("dtype,frac", [("float16", 0.05), ("bfloat16", 0.2)])
+def test_half_precision_engine_tracks_oracle(cuda, dtype, frac):
     """head_dim 64 in fp16 / bf16 runs the TMA/mma decode kernel and the tcgen05 prefill
-    kernel.  Half-precision activations move these logits (std ~4) by ~0.2 (fp16) /
-    ~0.6 (bf16) against the fp32 oracle, enough to flip near-ties, so the streams are
-    teacher-forced: the product engine is fed the oracle's tokens and every logit row
-    it produces must lie within ``tol`` of the oracle's, and its own argmax must equal
-    the oracle's token wherever the oracle's top-1/top-2 margin exceeds 2 * tol.
+    kernel.  Half-precision activations move the logits against the fp32 oracle by a
+    few percent of their spread (more for bf16's 8-bit mantissa), enough to flip
+    near-ties, so the streams are teacher-forced: the product engine is fed the
+    oracle's tokens, every logit row it produces must lie within ``frac`` times the
+    row's standard deviation of the oracle's row, and its own argmax must equal the
+    oracle's token wherever the oracle's top-1/top-2 margin exceeds twice that bound.
     Block reuse is on (a tight pool), as in the fp32 stream test.
     """
     from tinyvllm_b200.engine import LLMEngine, SamplingParams
-    model = _tiny(dtype, 256, 4, 2, seed=3)
+    model = _tiny(dtype, 256, 4, 2, seed=3, init_std=0.1)
     prompts, max_toks = _requests(2, 6, 97, 3, 150, 4, 16)
     exp, gaps = _run_oracle(model, prompts, max_toks, 3, 40, with_gaps=True)
     c = model.config
@@ -126,7 +127,8 @@ def test_half_precision_engine_tracks_oracle(cuda, dtype, tol):
         got_rows, exp_rows = Forced.recorded[rid], oracle_logits[rid]
         assert len(got_rows) == len(exp_rows)
         for k, (g, e) in enumerate(zip(got_rows, exp_rows)):
-            assert np.abs(g - e).max() <= tol, f"request {rid} token {k}: logits off by {np.abs(g - e).max()}"
+            tol = frac * float(np.std(e))
+            assert np.abs(g - e).max() <= tol, f"request {rid} token {k}: logits off by {np.abs(g - e).max()} > {tol}"
             if gaps[rid][k] > 2 * tol:
                 assert int(np.argmax(g)) == exp[rid][k]
                 n_checked += 1

@@ -146,6 +146,37 @@ def test_write_kv_slots_and_fused_rope(cuda, dtype):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("with_slots", [False, True])
+def test_qkv_rope_matches_separate_ops(cuda, dtype, with_slots):
+    """One packed projection row split + RoPE == slicing then tvk_rope (and tvk_write_kv_slots)."""
+    from tinyvllm_b200.layers import apply_rope_, precompute_freqs_cis, qkv_rope, write_kv_slots
+    g = _gen(cuda, 21)
+    T, hq, hkv, d = 13, 32, 8, 128
+    cols = (hq + 2 * hkv) * d
+    qkv = torch.randn(T, cols + 64, generator=g, device=cuda).to(dtype)[:, :cols]   # strided rows
+    pos = torch.randint(0, 512, (T,), generator=g, device=cuda, dtype=torch.int32)
+    cos, sin = precompute_freqs_cis(d, 1024, 5e5, cuda)
+    slots = torch.arange(3, 3 + T, dtype=torch.int64, device=cuda) if with_slots else None
+    kc = torch.zeros(4, 16, hkv, d, dtype=dtype, device=cuda)
+    vc = torch.zeros_like(kc)
+    q, k, v = qkv_rope(qkv, hq, hkv, d, cos, sin, pos, slots=slots, k_cache=kc, v_cache=vc)
+    q2 = qkv[:, :hq * d].reshape(T, hq, d).contiguous()
+    k2 = qkv[:, hq * d:(hq + hkv) * d].reshape(T, hkv, d).contiguous()
+    v2 = qkv[:, (hq + hkv) * d:].reshape(T, hkv, d).contiguous()
+    apply_rope_(q2, k2, cos, sin, pos)
+    torch.cuda.synchronize()
+    assert torch.equal(q, q2) and torch.equal(k, k2) and torch.equal(v, v2)
+    if with_slots:
+        kc2 = torch.zeros_like(kc)
+        vc2 = torch.zeros_like(kc)
+        write_kv_slots(k2, v2, slots, kc2, vc2)
+        torch.cuda.synchronize()
+        assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
+    else:
+        assert torch.count_nonzero(kc) == 0
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
 def test_silu_mul_packed_and_separate(cuda, dtype):
     from tinyvllm_b200.layers import silu_mul
     g = _gen(cuda, 11)

@@ -35,6 +35,7 @@ SIGNATURES = {
     "tvk_rope": (_c_int, [_c_void] * 5 + [_c_int] * 6 + [_c_void]),
     "tvk_rope_write_kv": (_c_int, [_c_void] * 9 + [_c_int] * 8 + [_c_void]),
     "tvk_write_kv_slots": (_c_int, [_c_void] * 5 + [_c_int] * 6 + [_c_void]),
+    "tvk_qkv_rope": (_c_int, [_c_void, _c_int64] + [_c_void] * 9 + [_c_int] * 8 + [_c_void]),
     "tvk_silu_mul": (_c_int, [_c_void] * 3 + [_c_int, _c_int, _c_int64, _c_int64, _c_int64, _c_int, _c_void]),
     "tvk_embedding": (_c_int, [_c_void] * 3 + [_c_int] * 4 + [_c_void, _c_void]),
     "tvk_argmax": (_c_int, [_c_void] * 2 + [_c_int, _c_int, _c_int64, _c_int, _c_void]),

@@ -6,6 +6,7 @@
 //   tvk_rope              apply_rope                   llama.py:34-55 (interleaved pairs, fp32 tables)
 //   tvk_write_kv_slots    KVCache.write_kv             core/kv_cache.py:34-38, decode append llama.py:381-386
 //   tvk_rope_write_kv     apply_rope on q and k, then the roped k and v stored into their paged slots
+//   tvk_qkv_rope          the same from one packed [q | k | v] projection row (one GEMM for q, k, v)
 //   tvk_silu_mul          FeedForward gate             llama.py:220-221
 //   tvk_embedding         Embedding row gather         llama.py:276,310
 //   tvk_argmax            greedy pick                  core/sampling.py:133-134 (first index on ties)
@@ -104,17 +105,22 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const T* __restr
 // ---------------------------------------------------------------------------
 // RoPE on interleaved pairs (x[2i], x[2i+1]) with fp32 cos/sin tables [max_pos, D/2]
 // ---------------------------------------------------------------------------
+// (x0, x1) -> (x0 c - x1 s, x0 s + x1 c), rounded product by product (no fused
+// multiply-add), the same in every kernel and as the reference's elementwise ops.
+__device__ __forceinline__ void rotate_pair(float& x0, float& x1, float c, float s) {
+  const float a = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+  const float b = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+  x0 = a;
+  x1 = b;
+}
+
 template <typename T>
 __device__ __forceinline__ void rope_vec(T* p, const float* c, const float* s) {
   constexpr int N = Vec<T>::N;
   float f[N];
   load_vec<T>(p, f);
 #pragma unroll
-  for (int e = 0; e < N; e += 2) {
-    const float x0 = f[e], x1 = f[e + 1], cc = c[e / 2], sn = s[e / 2];
-    f[e] = x0 * cc - x1 * sn;
-    f[e + 1] = x0 * sn + x1 * cc;
-  }
+  for (int e = 0; e < N; e += 2) rotate_pair(f[e], f[e + 1], c[e / 2], s[e / 2]);
   store_vec<T>(p, f);
 }
 
@@ -157,6 +163,58 @@ __global__ void rope_kernel(T* q, T* k, const T* v, const float* __restrict__ co
               *reinterpret_cast<const uint4*>(v + ((size_t)t * hkv + kh) * D + vi * N);
         }
       }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Packed projection rows [q | k | v] -> RoPE'd q and k and v as separate
+// contiguous tensors (optionally also the roped k and v into paged slots).
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void qkv_rope_kernel(const T* __restrict__ qkv, long long row_stride, T* __restrict__ q,
+                                T* __restrict__ k, T* __restrict__ v, const float* __restrict__ cos_t,
+                                const float* __restrict__ sin_t, const int32_t* __restrict__ pos, int n_tokens, int hq,
+                                int hkv, int D, int max_pos, const int64_t* __restrict__ slots, T* k_cache,
+                                T* v_cache, long long n_slots) {
+  constexpr int N = Vec<T>::N;
+  const int vpr = D / N;
+  const int heads = hq + 2 * hkv;
+  const long long total = (long long)n_tokens * heads * vpr;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int vi = (int)(i % vpr);
+    const long long th = i / vpr;
+    const int head = (int)(th % heads);
+    const int t = (int)(th / heads);
+    float f[N];
+    load_vec<T>(qkv + t * row_stride + (size_t)head * D + vi * N, f);
+    if (head < hq + hkv) {
+      int p = pos[t];
+      p = p < 0 ? 0 : (p >= max_pos ? max_pos - 1 : p);
+#pragma unroll
+      for (int e = 0; e < N; e += 2)
+        rotate_pair(f[e], f[e + 1], cos_t[(size_t)p * (D / 2) + vi * (N / 2) + e / 2],
+                    sin_t[(size_t)p * (D / 2) + vi * (N / 2) + e / 2]);
+    }
+    T* dst;
+    T* cache = nullptr;
+    int kvh = 0;
+    if (head < hq) {
+      dst = q + ((size_t)t * hq + head) * D;
+    } else if (head < hq + hkv) {
+      kvh = head - hq;
+      dst = k + ((size_t)t * hkv + kvh) * D;
+      cache = k_cache;
+    } else {
+      kvh = head - hq - hkv;
+      dst = v + ((size_t)t * hkv + kvh) * D;
+      cache = v_cache;
+    }
+    store_vec<T>(dst + vi * N, f);
+    if (slots && cache) {
+      const long long slot = slots[t];
+      if (slot >= 0 && slot < n_slots) store_vec<T>(cache + ((size_t)slot * hkv + kvh) * D + vi * N, f);
     }
   }
 }
@@ -375,6 +433,32 @@ extern "C" int tvk_rope_write_kv(void* q, void* k, const void* v, const float* c
       (T*)q, (T*)k, (const T*)v, cos_table, sin_table, positions, n_tokens, n_heads, n_kv_heads, head_dim, max_pos,
       slots, (T*)k_cache, (T*)v_cache, (long long)num_blocks * block_size));
   TVK_CHECK_LAUNCH("rope_write_kv");
+  return TVK_OK;
+}
+
+extern "C" int tvk_qkv_rope(const void* qkv, long long row_stride, void* q, void* k, void* v, const float* cos_table,
+                            const float* sin_table, const int32_t* positions, const int64_t* slots, void* k_cache,
+                            void* v_cache, int n_tokens, int n_heads, int n_kv_heads, int head_dim, int max_pos,
+                            int num_blocks, int block_size, int dtype, void* stream) {
+  TVK_CHECK_ARG(n_tokens >= 0, "negative n_tokens");
+  if (n_tokens == 0) return TVK_OK;
+  TVK_CHECK_ARG(qkv && q && k && v && cos_table && sin_table && positions, "null pointer argument");
+  const int N = vec_elems(dtype);
+  TVK_CHECK_ARG(head_dim % N == 0 && max_pos > 0 && row_stride % N == 0 &&
+                    row_stride >= (long long)(n_heads + 2 * n_kv_heads) * head_dim,
+                "bad shape (head_dim and row_stride multiples of %d, row_stride >= (n_heads + 2 n_kv_heads) head_dim)",
+                N);
+  TVK_CHECK_ARG(aligned16(qkv) && aligned16(q) && aligned16(k) && aligned16(v), "pointers must be 16-byte aligned");
+  if (slots) {
+    TVK_CHECK_ARG(k_cache && v_cache && num_blocks > 0 && block_size > 0 && aligned16(k_cache) && aligned16(v_cache),
+                  "slots need 16-byte aligned k_cache and v_cache, num_blocks and block_size");
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const long long work = (long long)n_tokens * (n_heads + 2 * n_kv_heads) * (head_dim / N);
+  TVK_DISPATCH(dtype, qkv_rope_kernel<T><<<grid_for(work, 256), 256, 0, s>>>(
+      (const T*)qkv, row_stride, (T*)q, (T*)k, (T*)v, cos_table, sin_table, positions, n_tokens, n_heads, n_kv_heads,
+      head_dim, max_pos, slots, (T*)k_cache, (T*)v_cache, slots ? (long long)num_blocks * block_size : 0));
+  TVK_CHECK_LAUNCH("qkv_rope");
   return TVK_OK;
 }
 

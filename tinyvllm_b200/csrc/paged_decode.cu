@@ -528,7 +528,7 @@ __global__ void __launch_bounds__(128) paged_decode_combine_kernel(const DecodeP
 // -----------------------------------------------------------------------------
 // host side
 // -----------------------------------------------------------------------------
-constexpr int kTargetCtas = 148 * 8;
+constexpr int kTargetCtas = 148 * 3;  // about one and a half waves of 2 CTAs per SM
 
 int table_tokens(int block_size, int max_blocks, int max_context_len) {
   int blocks = max_blocks;
@@ -540,7 +540,8 @@ int table_tokens(int block_size, int max_blocks, int max_context_len) {
 }
 
 // Tokens per CTA: the largest of 512/256/128/64 that still gives enough CTAs
-// to fill the GPU when every sequence uses its whole table.
+// to fill the GPU when every sequence uses its whole table.  Larger splits mean
+// fewer partials to merge and fewer CTAs that find no live token.
 int choose_split(int batch, int n_kv_heads, int max_ctx_tokens) {
   const long units = (long)batch * n_kv_heads;
   for (int s = 512; s > kStageTok; s >>= 1)

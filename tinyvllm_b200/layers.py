@@ -77,6 +77,33 @@ def apply_rope_write_kv_(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos:
     _lib.check(rc, "tvk_rope_write_kv")
 
 
+def qkv_rope(qkv: torch.Tensor, n_heads: int, n_kv_heads: int, head_dim: int, cos: torch.Tensor,
+             sin: torch.Tensor, positions: torch.Tensor, *, slots: Optional[torch.Tensor] = None,
+             k_cache: Optional[torch.Tensor] = None, v_cache: Optional[torch.Tensor] = None,
+             out: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None):
+    """Split packed projection rows ``qkv`` [T, >= (Hq+2Hkv)*D] (one GEMM against
+    wq|wk|wv, llama.py:174-176) into contiguous q [T,Hq,D], k, v [T,Hkv,D] with RoPE
+    on q and k (llama.py:178-179); with ``slots`` the roped k and v also go to the pool."""
+    dev = _lib.require_cuda(qkv, cos, sin, positions, *(t for t in (slots, k_cache, v_cache) if t is not None))
+    if qkv.stride(-1) != 1 or qkv.dim() != 2:
+        raise ValueError("qkv must be [T, C] with contiguous rows")
+    T = qkv.shape[0]
+    if out is None:
+        q = torch.empty(T, n_heads, head_dim, dtype=qkv.dtype, device=qkv.device)
+        k = torch.empty(T, n_kv_heads, head_dim, dtype=qkv.dtype, device=qkv.device)
+        v = torch.empty(T, n_kv_heads, head_dim, dtype=qkv.dtype, device=qkv.device)
+    else:
+        q, k, v = out
+    nb = k_cache.shape[0] if k_cache is not None else 0
+    bs = k_cache.shape[1] if k_cache is not None else 0
+    rc = _lib.lib().tvk_qkv_rope(_lib.ptr(qkv), qkv.stride(0), _lib.ptr(q), _lib.ptr(k), _lib.ptr(v), _lib.ptr(cos),
+                                 _lib.ptr(sin), _lib.ptr(positions), _lib.ptr(slots), _lib.ptr(k_cache),
+                                 _lib.ptr(v_cache), T, n_heads, n_kv_heads, head_dim, cos.shape[0], nb, bs,
+                                 _lib.dtype_code(qkv), _stream(dev))
+    _lib.check(rc, "tvk_qkv_rope")
+    return q, k, v
+
+
 def write_kv_slots(k: torch.Tensor, v: torch.Tensor, slots: torch.Tensor, k_cache: torch.Tensor,
                    v_cache: torch.Tensor) -> None:
     """KVCache.write_kv for a batch of rows (core/kv_cache.py:34-38): k/v [T,Hkv,D] ->

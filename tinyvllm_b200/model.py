@@ -78,9 +78,7 @@ def llama3_8b_config(dtype: str = "bfloat16") -> LlamaConfig:
 @dataclass
 class LayerWeights:
     attention_norm: torch.Tensor
-    wq: torch.Tensor
-    wk: torch.Tensor
-    wv: torch.Tensor
+    wqkv: torch.Tensor    # [dim, (n_heads + 2 n_kv_heads) * head_dim]: wq | wk | wv columns
     wo: torch.Tensor
     ffn_norm: torch.Tensor
     w13: torch.Tensor     # [dim, 2*hidden]: gate (w1) columns then up (w3) columns
@@ -142,7 +140,7 @@ class Llama:
         for _ in range(c.n_layers):
             self.layers.append(LayerWeights(
                 attention_norm=torch.ones(c.dim, dtype=dt, device=self.device),
-                wq=rnd(c.dim, c.n_heads * D), wk=rnd(c.dim, c.n_kv_heads * D), wv=rnd(c.dim, c.n_kv_heads * D),
+                wqkv=rnd(c.dim, (c.n_heads + 2 * c.n_kv_heads) * D),
                 wo=rnd(c.n_heads * D, c.dim),
                 ffn_norm=torch.ones(c.dim, dtype=dt, device=self.device),
                 w13=rnd(c.dim, 2 * c.hidden_dim), w2=rnd(c.hidden_dim, c.dim)))
@@ -155,12 +153,16 @@ class Llama:
         """All weights as float32 numpy arrays (for the CPU oracle)."""
         f = lambda t: t.float().cpu().numpy()
         w = {"tok_embeddings": f(self.tok_embeddings), "norm": f(self.norm), "output": f(self.output)}
-        H = self.config.hidden_dim
+        c = self.config
+        H = c.hidden_dim
+        nq, nk = c.n_heads * c.head_dim, c.n_kv_heads * c.head_dim
         for i, L in enumerate(self.layers):
             w13 = f(L.w13)
-            w.update({f"l{i}.attention_norm": f(L.attention_norm), f"l{i}.wq": f(L.wq), f"l{i}.wk": f(L.wk),
-                      f"l{i}.wv": f(L.wv), f"l{i}.wo": f(L.wo), f"l{i}.ffn_norm": f(L.ffn_norm),
-                      f"l{i}.w1": w13[:, :H], f"l{i}.w3": w13[:, H:], f"l{i}.w2": f(L.w2)})
+            wqkv = f(L.wqkv)
+            w.update({f"l{i}.attention_norm": f(L.attention_norm), f"l{i}.wq": wqkv[:, :nq],
+                      f"l{i}.wk": wqkv[:, nq:nq + nk], f"l{i}.wv": wqkv[:, nq + nk:], f"l{i}.wo": f(L.wo),
+                      f"l{i}.ffn_norm": f(L.ffn_norm), f"l{i}.w1": w13[:, :H], f"l{i}.w3": w13[:, H:],
+                      f"l{i}.w2": f(L.w2)})
         return w
 
     # ------------------------------------------------------------------ blocks
@@ -174,12 +176,15 @@ class Llama:
         f = torch.matmul(a, L.w2)
         return layers.rms_norm(f, next_norm, c.norm_eps, residual=h)     # h += f; x = next_norm(h)
 
-    def _qkv(self, L: LayerWeights, x: torch.Tensor, T: int):
+    def _qkv(self, L: LayerWeights, x: torch.Tensor, positions: torch.Tensor, slots=None, kv_cache=None, i=0):
+        """One GEMM against wq|wk|wv, then RoPE'd q, k and v split out by one kernel
+        (with ``slots`` the roped k and v are also stored to layer ``i``'s pool)."""
         c = self.config
-        q = torch.matmul(x, L.wq).view(T, c.n_heads, c.head_dim)
-        k = torch.matmul(x, L.wk).view(T, c.n_kv_heads, c.head_dim)
-        v = torch.matmul(x, L.wv).view(T, c.n_kv_heads, c.head_dim)
-        return q, k, v
+        qkv = torch.matmul(x, L.wqkv)
+        kc = kv_cache.k_cache[i] if slots is not None else None
+        vc = kv_cache.v_cache[i] if slots is not None else None
+        return layers.qkv_rope(qkv, c.n_heads, c.n_kv_heads, c.head_dim, self.cos, self.sin, positions,
+                               slots=slots, k_cache=kc, v_cache=vc)
 
     # ---------------------------------------------------------------- prefill
     def prefill(self, tokens: torch.Tensor, positions: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int,
@@ -195,8 +200,7 @@ class Llama:
         h = layers.embedding(self.tok_embeddings, tokens)
         x = layers.rms_norm(h, self.layers[0].attention_norm, c.norm_eps)
         for i, L in enumerate(self.layers):
-            q, k, v = self._qkv(L, x, T)
-            layers.apply_rope_(q, k, self.cos, self.sin, positions)
+            q, k, v = self._qkv(L, x, positions)
             attn = flash_prefill_attention_varlen(q, k, v, cu_seqlens, max_seqlen, True, slot_mapping=slot_mapping,
                                                   k_cache=kv_cache.k_cache[i], v_cache=kv_cache.v_cache[i])
             nxt = self.layers[i + 1].attention_norm if i + 1 < c.n_layers else self.norm
@@ -225,12 +229,11 @@ class Llama:
         h = layers.embedding(self.tok_embeddings, tokens)
         x = layers.rms_norm(h, self.layers[0].attention_norm, c.norm_eps)
         for i, L in enumerate(self.layers):
-            q, k, v = self._qkv(L, x, B)
             kc, vc = kv_cache.k_cache[i], kv_cache.v_cache[i]
             if kv_order == "append_first":
-                layers.apply_rope_write_kv_(q, k, v, self.cos, self.sin, positions, slots, kc, vc)
+                q, k, v = self._qkv(L, x, positions, slots, kv_cache, i)
             else:
-                layers.apply_rope_(q, k, self.cos, self.sin, positions)
+                q, k, v = self._qkv(L, x, positions)
             attn = paged_decode_attention(q.view(B, 1, c.n_heads, c.head_dim), kc, vc, block_tables, context_lens,
                                           c.n_heads, c.n_kv_heads, c.head_dim, kv_cache.block_size)
             if kv_order != "append_first":
