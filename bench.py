@@ -24,6 +24,7 @@ installable in this image), on a bounded sample of the same workload.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -258,8 +259,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
         avg_launch_ms = statistics.mean(per_step)
         achieved = alg / (avg_launch_ms / 1e3) / 1e9
         L = _lib.lib()
-        ws = L.tvk_paged_decode_workspace_size(B, 32, 8, 128, 16, case.block_tables.shape[1], -1)
-        launches_per_step = 2 if ws > 256 else 1
+        plan = (ctypes.c_int * 4)()
+        _lib.check(L.tvk_paged_decode_plan(B, 32, 8, 128, 16, case.block_tables.shape[1], -1, 1, plan),
+                   "tvk_paged_decode_plan")
+        launches_per_step = plan[2]
         traffic_path = ROOT / "profiles" / "paged_decode_tc_config3.traffic.json"
         traffic = None
         if traffic_path.exists():
@@ -280,7 +283,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": alg,
                          "avg_step_ms": avg_launch_ms,
-                         "note": "per-step events bracket the whole call (main kernel + split-K combine)"},
+                         "note": "per-step events bracket the whole call (main kernel, plus the split-K combine when the plan has one)",
+                         "unit_tokens": plan[0], "max_splits": plan[1], "persistent": bool(plan[3])},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms / args.steps},

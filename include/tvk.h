@@ -45,12 +45,29 @@ const char* tvk_last_error(void);
 
 /*
  * Bytes of scratch that tvk_paged_decode_attention needs for a batch whose
- * block tables are `max_blocks` wide: a 256-byte header (a device status word)
- * followed by the split-K partials (fp32 output rows plus max / sum pairs).
+ * block tables are `max_blocks` wide: a 256-byte header (a device status word
+ * at byte 0, work-list counters at bytes 64 and 128, the unit size of the last
+ * call at byte 192) followed by the split-K partials (fp32 output rows plus
+ * max / sum pairs).  Zero the header once after allocating the workspace;
+ * every call returns the status word and the counters to zero unless a
+ * kernel wait timed out.  One workspace serves one stream at a time.
  * Replaces nothing in the reference (tinygrad allocates its temporaries).
  */
 size_t tvk_paged_decode_workspace_size(int batch, int n_heads, int n_kv_heads, int head_dim,
                                        int block_size, int max_blocks, int max_context_len);
+
+/*
+ * How tvk_paged_decode_attention cuts and launches a call with these sizes
+ * (nothing is launched here).  plan_out[0] = the smallest unit of context
+ * tokens (one unit = one split of one (sequence, KV head)); plan_out[1] = the
+ * most splits a sequence may take; plan_out[2] = kernel launches per call
+ * (2 when a split-K combine follows); plan_out[3] = 1 when persistent CTAs
+ * take units from the workspace's ticket counter and size them from the live
+ * contexts (units then hold at least plan_out[0] tokens), 0 when every unit
+ * gets its own CTA.  No counterpart in the reference.
+ */
+int tvk_paged_decode_plan(int batch, int n_heads, int n_kv_heads, int head_dim, int block_size,
+                          int max_blocks, int max_context_len, int dtype, int* plan_out);
 
 /*
  * Paged-decode attention, one query token per sequence.

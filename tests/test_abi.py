@@ -73,8 +73,30 @@ def test_workspace_size_arithmetic(lib):
     assert lib.tvk_paged_decode_workspace_size(4096, 32, 8, 128, 16, 4, -1) == hdr
     # max_context_len truncates the table
     a = lib.tvk_paged_decode_workspace_size(256, 32, 8, 128, 16, 256, -1)
-    b = lib.tvk_paged_decode_workspace_size(256, 32, 8, 128, 16, 256, 1024)
-    assert b < a
+    b = lib.tvk_paged_decode_workspace_size(256, 32, 8, 128, 16, 256, 48)
+    assert b == hdr < a
+
+
+def test_decode_plan(lib):
+    plan = (ctypes.c_int * 4)()
+    # config 3: 256 sequences x 8 KV heads, 4096-token tables -> persistent CTAs,
+    # one 4096-token unit per (sequence, KV head), no combine
+    assert lib.tvk_paged_decode_plan(256, 32, 8, 128, 16, 256, -1, 1, plan) == 0
+    assert list(plan) == [4096, 1, 1, 1]
+    # engine-sized call (64 sequences x 4 KV heads, 64-block tables): one CTA per
+    # 512-token unit, a combine for the second split
+    assert lib.tvk_paged_decode_plan(64, 32, 4, 64, 16, 64, -1, 1, plan) == 0
+    assert list(plan) == [512, 2, 2, 0]
+    # fp32 always takes the one-CTA-per-unit kernel
+    assert lib.tvk_paged_decode_plan(256, 32, 8, 128, 16, 256, -1, 0, plan) == 0
+    assert plan[3] == 0
+    # the workspace covers every plan the sizes can take
+    for dt in (0, 1, 2):
+        for args in ((256, 32, 8, 128, 16, 256, -1), (64, 32, 4, 64, 16, 64, -1), (4, 32, 4, 64, 16, 16, -1)):
+            assert lib.tvk_paged_decode_plan(*args, dt, plan) == 0
+            need = 256 + (args[0] * args[1] * plan[1] * (args[3] + 2) * 4 if plan[1] > 1 else 0)
+            assert lib.tvk_paged_decode_workspace_size(*args) >= need
+    assert lib.tvk_paged_decode_plan(0, 32, 8, 128, 16, 256, -1, 1, plan) == -1
 
 
 def test_invalid_arguments_are_rejected_before_any_launch(lib):

@@ -211,3 +211,53 @@ def test_repeat_calls_are_deterministic(cuda):
     a = _run(case).clone()
     b = _run(case)
     assert torch.equal(a, b)
+
+
+def _call_abi(case, ws, nbytes):
+    from tinyvllm_b200 import _lib
+    out = torch.empty_like(case.q)
+    rc = _lib.lib().tvk_paged_decode_attention(
+        case.q.data_ptr(), case.k_cache.data_ptr(), case.v_cache.data_ptr(), case.block_tables.data_ptr(),
+        case.context_lens.data_ptr(), out.data_ptr(), case.batch, case.n_heads, case.n_kv_heads, case.head_dim,
+        case.block_size, case.k_cache.shape[0], case.block_tables.shape[1], -1, _lib.dtype_code(case.q),
+        None if ws is None else ws.data_ptr(), nbytes, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, _lib.lib().tvk_last_error()
+    torch.cuda.synchronize()
+    return out
+
+
+def test_work_list_counters_return_to_zero(cuda):
+    """The tensor-core kernel hands out its (sequence, KV head, split) units from
+    counters in the workspace header (status word at byte 0, counters at 64 and
+    128); every call leaves them zeroed, so back-to-back calls on one workspace
+    give identical results.  Bytes 192.. hold the unit size of the last call."""
+    from tinyvllm_b200 import _lib, workloads
+    case = workloads.decode_config3(cuda, batch=96)
+    n = _lib.lib().tvk_paged_decode_workspace_size(case.batch, 32, 8, 128, 16, case.block_tables.shape[1], -1)
+    ws = torch.zeros(n, dtype=torch.uint8, device=cuda)
+    outs = [_call_abi(case, ws, n).clone() for _ in range(3)]
+    assert torch.count_nonzero(ws[:192]) == 0
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+    _check(outs[0][:8], _oracle_rows(case, range(8)), torch.float16)
+
+
+def _oracle_rows(case, idx):
+    idx = list(idx)
+    return oa.paged_decode_attention(_np(case.q[idx]), _np(case.k_cache), _np(case.v_cache),
+                                     case.block_tables[idx].cpu().numpy(), case.context_lens[idx].cpu().numpy(),
+                                     case.n_heads, case.n_kv_heads, case.head_dim, case.block_size)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_without_workspace_matches_with(cuda, dtype):
+    """Single-split batches may pass no workspace: the units then go to CTAs in a
+    fixed order instead of from the header counters; results are the same."""
+    from tinyvllm_b200 import workloads
+    ctx = [1, 17, 64, 5, 2, 33, 48, 63] * 40
+    case = workloads.decode_case(len(ctx), 32, 8, 128, 16, ctx, dtype=dtype, device=cuda, seed=21, width=4,
+                                 contiguous=True)
+    a = _call_abi(case, None, 0)
+    ws = torch.zeros(1 << 16, dtype=torch.uint8, device=cuda)
+    b = _call_abi(case, ws, ws.numel())
+    assert torch.equal(a, b)
+    _check(a, _oracle(case), dtype)

@@ -25,6 +25,7 @@ SIGNATURES = {
     "tvk_abi_version": (_c_int, []),
     "tvk_last_error": (ctypes.c_char_p, []),
     "tvk_paged_decode_workspace_size": (_c_size, [_c_int] * 7),
+    "tvk_paged_decode_plan": (_c_int, [_c_int] * 8 + [_c_void]),
     "tvk_paged_decode_attention": (
         _c_int,
         [_c_void] * 6 + [_c_int] * 9 + [_c_void, _c_size, _c_void],

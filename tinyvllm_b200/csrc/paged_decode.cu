@@ -3,19 +3,22 @@
 // Replaces paged_decode_attention (tinyvllm/model/llama.py:97-144).  The
 // reference gathers every table entry into a dense [B, maxctx, Hkv, D] copy,
 // materialises the GQA expand and runs two batched matmuls over the padded
-// length.  Here each CTA owns one (sequence, KV head, context split) and reads
-// only the blocks that hold live tokens, once, for all n_heads/n_kv_heads query
-// heads that share that KV head.
+// length.  Here the work is cut into units of one (sequence, KV head, context
+// split); a unit reads only the blocks that hold live tokens, once, for all
+// n_heads/n_kv_heads query heads that share that KV head.
 //
 // Two kernels:
 //  * tc  (fp16 / bf16, block_size in {8,16,32,64}, head_dim in {32,64,128}):
-//    one producer warp issues 4-D TMA loads of whole K/V blocks (one KV head,
+//    persistent CTAs, about two per SM, take units from an atomic counter.
+//    One producer warp issues 4-D TMA loads of whole K/V blocks (one KV head,
 //    all block_size rows, swizzled) into a multi-stage shared-memory ring
-//    guarded by mbarriers; four consumer warps each take 16 tokens of a stage
-//    and run Q.K^T and P.V on the tensor cores (m16n8k16, fp32 accumulate) with
-//    the GQA group as the M dimension, and an fp32 online softmax in registers.
-//  * simt (any dtype incl. fp32, any block size): cooperative vector loads of
-//    32-token tiles into shared memory and fp32 CUDA-core math.
+//    guarded by mbarriers that runs on across unit boundaries; four consumer
+//    warps each take 16 tokens of a stage and run Q.K^T and P.V on the tensor
+//    cores (m16n8k16, fp32 accumulate) with the GQA group as the M dimension,
+//    and an fp32 online softmax in registers.
+//  * simt (any dtype incl. fp32, any block size): one CTA per unit,
+//    cooperative vector loads of 32-token tiles into shared memory and fp32
+//    CUDA-core math.
 // Sequences longer than one split are reduced by a small combine kernel from
 // fp32 partials (max, sum, unnormalised output) kept in the caller workspace.
 #include <math.h>
@@ -40,9 +43,12 @@ struct DecodeParams {
   float* part_o;        // [B, Hq, max_splits, D]
   float* part_ml;       // [B, Hq, max_splits, 2]
   int* status;          // may be null
+  uint8_t* sched;       // workspace header (work-list counters); null: static unit order
   int batch, n_heads, n_kv_heads, group, head_dim, block_size, num_blocks, max_blocks;
   int max_ctx_tokens;  // (possibly truncated) table width * block_size
-  int split_tokens;    // tokens per CTA, multiple of kStageTok
+  int split_tokens;    // tokens per unit (the smallest the call may use), multiple of kStageTok
+  int device_split;    // 1: the tc kernel picks the unit size from the live contexts
+  int dynamic;         // 1: tc CTAs past their first unit take tickets from the workspace counter
   int max_splits;
   float scale_log2;  // log2(e) / sqrt(head_dim)
 };
@@ -87,12 +93,74 @@ struct TcCfg {
   static constexpr int kStageBytes = 2 * kKVBytes;
   static constexpr int kStages = D == 128 ? 3 : (D == 64 ? 5 : 8);
   static constexpr int kRingBytes = kStages * kStageBytes;
-  static constexpr int kCombineBytes = 4 * kMaxGroup * (D + 2) * 4;
-  static constexpr int kBodyBytes = kRingBytes > kCombineBytes ? kRingBytes : kCombineBytes;
-  static constexpr int kBarOffset = kBodyBytes;
-  static constexpr int kSmemBytes = kBarOffset + 2 * kStages * 8 + 1024;  // +1024 alignment slack
+  static constexpr int kBarOffset = kRingBytes;             // full / empty barriers
+  static constexpr int kMetaOffset = kRingBytes + 128;      // one int4 of unit data per stage
+  static constexpr int kQOffset = kRingBytes + 256;         // one query slot [group][D] per stage
+  static_assert(2 * kStages * 8 <= 128 && kStages * 16 <= 128, "barrier / meta area");
+  // merge scratch of the four consumer warps: m, l [4][16] then O [4][group][D]
+  static __host__ __device__ constexpr int merge_offset(int group) { return kQOffset + kStages * group * D * 2; }
+  static __host__ __device__ constexpr int smem_bytes(int group) {
+    return merge_offset(group) + 2 * 4 * 16 * 4 + 4 * group * D * 4 + 1024;  // +1024 alignment slack
+  }
 };
 
+// Work-list counters in the caller workspace header (the status word is at 0),
+// and the unit size the last tc launch chose (read by the combine kernel).
+constexpr int kTicketOffset = 64;
+constexpr int kDoneOffset = 128;
+constexpr int kSplitOffset = 192;
+
+// Resident tc CTAs on a B200 (two per SM), and the unit counts the split
+// policies aim for: about one and a half waves when every unit gets its own
+// CTA; about four units per resident CTA for persistent grids, enough for the
+// ticket counter to even out ragged contexts while keeping units long.
+constexpr long kSlots = 148L * 2;
+constexpr long kStaticTarget = 148L * 3;
+constexpr long kTargetUnits = kSlots * 4;
+constexpr int kMaxSplitTokens = 4096;
+
+// One unit of decode work: one context split of one (sequence, KV head).
+// Tickets run over splits slowest, so every CTA sees a mix of sequences and
+// the short tail splits of the longest sequences come last.
+struct Unit {
+  int b, kvh, split, n_tok, nsplit;
+};
+
+// Unit of ticket t; false if that split holds no live token.  A sequence with
+// no context is one unit (split 0) with n_tok 0 whose output rows are zeros.
+__device__ __forceinline__ bool decode_unit(const DecodeParams& p, int split_tokens, int t, Unit& un) {
+  const int bk_count = p.batch * p.n_kv_heads;
+  un.split = t / bk_count;
+  const int bk = t - un.split * bk_count;
+  un.kvh = bk % p.n_kv_heads;
+  un.b = bk / p.n_kv_heads;
+  const int ctx = effective_ctx(p, un.b);
+  if (ctx <= 0) {
+    un.n_tok = un.nsplit = 0;
+    return un.split == 0;
+  }
+  const int tok_begin = un.split * split_tokens;
+  if (tok_begin >= ctx) return false;
+  un.n_tok = min(split_tokens, ctx - tok_begin);
+  un.nsplit = (ctx + split_tokens - 1) / split_tokens;
+  return true;
+}
+
+__device__ __forceinline__ void unit_of_ticket(const DecodeParams& p, int t, Unit& un) {
+  const int bk_count = p.batch * p.n_kv_heads;
+  un.split = t / bk_count;
+  const int bk = t - un.split * bk_count;
+  un.kvh = bk % p.n_kv_heads;
+  un.b = bk / p.n_kv_heads;
+}
+
+// Persistent CTAs (about two per SM).  The producer warp takes units from an
+// atomic ticket counter (a fixed stride over tickets when no workspace is
+// given) and streams their K/V blocks through one TMA ring that runs across
+// unit boundaries, so the next unit's blocks are in flight while the consumers
+// merge and store the previous one.  Each stage carries the unit's ticket,
+// its stage index and token count, and on a unit's first stage its query rows,
+// so the consumer warps read nothing from global memory but the K/V stages.
 template <typename T, int D, int RB>
 __global__ void __launch_bounds__(160, 2)
     paged_decode_tc_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap tm_k,
@@ -100,19 +168,9 @@ __global__ void __launch_bounds__(160, 2)
   using C = TcCfg<D, RB>;
   constexpr int RC = RB / 2;  // elements per row chunk
   constexpr int K16_PER_ROW = RB / 16;
-
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-  const int ctx = effective_ctx(p, b);
-  if (ctx <= 0) {
-    if (split == 0) write_zero_rows<T>(p, b, kvh);
-    return;
-  }
-  const int tok_begin = split * p.split_tokens;
-  if (tok_begin >= ctx) return;
-  const int n_tok = min(p.split_tokens, ctx - tok_begin);
-  const int n_iters = (n_tok + kStageTok - 1) / kStageTok;
-  const int nsplit = (ctx + p.split_tokens - 1) / p.split_tokens;
   const int bs = p.block_size;
+  const int G = p.group;
+  const int total = p.batch * p.n_kv_heads * p.max_splits;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = ptx::smem_u32(smem_raw);
@@ -120,6 +178,9 @@ __global__ void __launch_bounds__(160, 2)
   uint8_t* base = smem_raw + (base_u32 - raw_u32);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(base + C::kBarOffset);
   uint64_t* empty_bar = full_bar + C::kStages;
+  int4* meta = reinterpret_cast<int4*>(base + C::kMetaOffset);
+  uint8_t* qslot = base + C::kQOffset;
+  const int q_bytes = G * D * 2;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -132,34 +193,162 @@ __global__ void __launch_bounds__(160, 2)
   __syncthreads();
 
   if (warp == 4) {
-    // ---------------- producer warp: TMA loads of whole K/V blocks ----------
+    // ---------------- producer warp ----------------------------------------
     if (lane == 0) {
       ptx::prefetch_tmap(&tm_k);
       ptx::prefetch_tmap(&tm_v);
     }
-    const int32_t* bt = p.block_tables + (size_t)b * p.max_blocks;
-    for (int it = 0; it < n_iters; ++it) {
-      const int s = it % C::kStages;
-      const uint32_t ph = (it / C::kStages) & 1;
-      if (!ptx::mbar_wait(&empty_bar[s], ph ^ 1)) {
-        report_timeout(p.status);
-        return;
+    // CTA i starts with ticket i; later tickets come from the counter (offset
+    // by the grid size) or, without it, in steps of the grid size.
+    unsigned* ticket = (p.sched && p.dynamic) ? reinterpret_cast<unsigned*>(p.sched + kTicketOffset) : nullptr;
+
+    // Unit size of this call: the largest power of two (<= 4096, >= the host's
+    // split) that still gives about kTargetUnits live units.  Every CTA reads
+    // the same contexts and reaches the same answer.
+    int split_tokens = p.split_tokens;
+    int live_total = total;
+    if (p.device_split) {
+      constexpr int NS = 7;  // 4096 .. 64
+      int cnt[NS];
+#pragma unroll
+      for (int k = 0; k < NS; ++k) cnt[k] = 0;
+      int max_ctx = 0;
+      for (int b = lane; b < p.batch; b += 32) {
+        const int c = effective_ctx(p, b);
+        if (c > 0) {
+          max_ctx = max(max_ctx, c);
+#pragma unroll
+          for (int k = 0; k < NS; ++k) cnt[k] = min(cnt[k] + ((c + (kMaxSplitTokens >> k) - 1) >> (12 - k)), 1 << 24);
+        }
       }
-      const int tok0 = tok_begin + it * kStageTok;  // absolute token of stage row 0
-      const int live = min(kStageTok, ctx - tok0);
-      const int nblk = (live + bs - 1) / bs;
-      if (lane == 0) ptx::mbar_arrive_expect_tx(&full_bar[s], (uint32_t)(nblk * bs * D * 2 * 2));
-      __syncwarp();
-      const uint32_t stage_off = s * C::kStageBytes;
-      const int n_loads = nblk * C::kChunks * 2;
-      for (int i = lane; i < n_loads; i += 32) {
-        const int j = i / (C::kChunks * 2);
-        const int rest = i % (C::kChunks * 2);
-        const int kv = rest / C::kChunks;
-        const int c = rest % C::kChunks;
-        const int blk = __ldg(bt + tok0 / bs + j);
-        uint8_t* dst = base + stage_off + kv * C::kKVBytes + c * C::kChunkBytes + j * bs * RB;
-        ptx::tma_load_4d(dst, kv ? &tm_v : &tm_k, &full_bar[s], c * RC, kvh, 0, blk);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {
+        max_ctx = max(max_ctx, __shfl_xor_sync(0xffffffffu, max_ctx, off));
+#pragma unroll
+        for (int k = 0; k < NS; ++k) cnt[k] += __shfl_xor_sync(0xffffffffu, cnt[k], off);
+      }
+#pragma unroll
+      for (int k = 0; k < NS; ++k) {
+        const int sk = kMaxSplitTokens >> k;
+        if (sk < p.split_tokens) break;
+        split_tokens = sk;
+        if ((long)cnt[k] * p.n_kv_heads >= kTargetUnits) break;
+      }
+      const int splits = max_ctx > 0 ? (max_ctx + split_tokens - 1) / split_tokens : 1;
+      live_total = p.batch * p.n_kv_heads * splits;
+      if (blockIdx.x == 0 && lane == 0 && p.sched) *reinterpret_cast<int*>(p.sched + kSplitOffset) = split_tokens;
+    }
+
+    // One atomic per claimed ticket.  A dead ticket (a split past its
+    // sequence's context) starts a scan: the lanes test the following
+    // (split, sequence) pairs 32 at a time and the counter is raised past the
+    // dead run in one atomicMax, so runs of dead tickets cost a few round trips
+    // instead of one atomic each.
+    int next_static = blockIdx.x;
+    uint32_t it_g = 0;
+    bool running = true;
+    const int bk_count = p.batch * p.n_kv_heads;
+    while (running) {
+      // next live unit (or the end of the list)
+      int t = total;
+      Unit un;
+      while (true) {
+        if (!ticket || next_static == (int)blockIdx.x) {
+          t = next_static;
+          next_static += gridDim.x;
+        } else {
+          int v = 0;
+          if (lane == 0) v = (int)atomicAdd(ticket, 1u);
+          t = __shfl_sync(0xffffffffu, v, 0) + (int)gridDim.x;
+        }
+        if (t >= live_total) {
+          t = total;
+          break;
+        }
+        if (decode_unit(p, split_tokens, t, un)) break;
+        if (!ticket) continue;
+        // Dead: every ticket of this (split, sequence) is dead; scan onwards.
+        // Split 0 is always live, so the scan runs over splits >= 1 only.
+        const int c_end = (live_total / bk_count) * p.batch;
+        int c = (t / bk_count) * p.batch + (t % bk_count) / p.n_kv_heads + 1;
+        int found = -1;
+        while (c < c_end) {
+          const int ci = c + lane;
+          bool ok = false;
+          if (ci < c_end) {
+            const int lvl = ci / p.batch;
+            ok = effective_ctx(p, ci - lvl * p.batch) > lvl * split_tokens;
+          }
+          const uint32_t m = __ballot_sync(0xffffffffu, ok);
+          if (m) {
+            found = c + __ffs(m) - 1;
+            break;
+          }
+          c += 32;
+        }
+        if (found < 0) {  // nothing live after t: the list is done
+          t = total;
+          break;
+        }
+        const int t_live = (found / p.batch) * bk_count + (found % p.batch) * p.n_kv_heads;
+        if (lane == 0 && t_live > (int)gridDim.x) atomicMax(ticket, (unsigned)(t_live - (int)gridDim.x));
+      }
+      const bool live = t < total;
+      running = live;
+      const int n_stage = live ? max((un.n_tok + kStageTok - 1) / kStageTok, 1) : 1;
+      const int tok_begin = live ? un.split * split_tokens : 0;
+      const int ctx_end = live ? tok_begin + un.n_tok : 0;
+      const int32_t* bt = live ? p.block_tables + (size_t)un.b * p.max_blocks : p.block_tables;
+      for (int it = 0; it < n_stage; ++it, ++it_g) {
+        const int s = it_g % C::kStages;
+        const uint32_t ph = (it_g / C::kStages) & 1;
+        if (!ptx::mbar_wait(&empty_bar[s], ph ^ 1)) {
+          report_timeout(p.status);
+          running = false;
+          break;
+        }
+        if (!live || un.n_tok == 0) {
+          // end of the list, or a sequence without context: no data
+          if (lane == 0) {
+            meta[s] = make_int4(live ? t : -1, 0, 0, 0);
+            ptx::mbar_arrive(&full_bar[s]);
+          }
+          continue;
+        }
+        const int tok0 = tok_begin + it * kStageTok;  // absolute token of stage row 0
+        const int live_tok = min(kStageTok, ctx_end - tok0);
+        const int nblk = (live_tok + bs - 1) / bs;
+        const uint32_t q_tx = it == 0 ? (uint32_t)q_bytes : 0u;
+        if (lane == 0) {
+          meta[s] = make_int4(t, it, un.n_tok, un.nsplit);
+          ptx::mbar_arrive_expect_tx(&full_bar[s], (uint32_t)(nblk * bs * D * 2 * 2) + q_tx);
+          if (it == 0) {
+            const uint8_t* qsrc = reinterpret_cast<const uint8_t*>(p.q) +
+                                  ((size_t)un.b * p.n_heads + (size_t)un.kvh * G) * D * 2;
+            ptx::bulk_load(qslot + s * q_bytes, qsrc, (uint32_t)q_bytes, &full_bar[s]);
+          }
+        }
+        __syncwarp();
+        const uint32_t stage_off = s * C::kStageBytes;
+        const int n_loads = nblk * C::kChunks * 2;
+        for (int i = lane; i < n_loads; i += 32) {
+          const int j = i / (C::kChunks * 2);
+          const int rest = i % (C::kChunks * 2);
+          const int kv = rest / C::kChunks;
+          const int c = rest % C::kChunks;
+          const int blk = __ldg(bt + tok0 / bs + j);
+          uint8_t* dst = base + stage_off + kv * C::kKVBytes + c * C::kChunkBytes + j * bs * RB;
+          ptx::tma_load_4d(dst, kv ? &tm_v : &tm_k, &full_bar[s], c * RC, un.kvh, 0, blk);
+        }
+      }
+    }
+    // Last CTA out returns the counters to zero for the next call.
+    if (ticket && lane == 0) {
+      unsigned* done = reinterpret_cast<unsigned*>(p.sched + kDoneOffset);
+      __threadfence();
+      if (atomicAdd(done, 1u) == gridDim.x - 1) {
+        atomicExch(ticket, 0u);
+        atomicExch(done, 0u);
       }
     }
     return;
@@ -167,37 +356,54 @@ __global__ void __launch_bounds__(160, 2)
 
   // ---------------- consumer warps ----------------------------------------
   const int g = lane >> 2, tig = lane & 3;
-  const int G = p.group;
+  float* cm = reinterpret_cast<float*>(base + C::merge_offset(G));
+  float* cl = cm + 4 * 16;
+  float* co = cl + 4 * 16;
 
-  // Q fragments (A operand, rows = query heads of this KV group, zero padded).
   uint32_t qa[D / 16][4];
-  {
-    const T* q = reinterpret_cast<const T*>(p.q) + ((size_t)b * p.n_heads + kvh * G) * D;
-    const uint32_t* q32 = reinterpret_cast<const uint32_t*>(q);
-#pragma unroll
-    for (int kk = 0; kk < D / 16; ++kk) {
-      const int c0 = kk * 16 + tig * 2;
-      qa[kk][0] = g < G ? q32[(g * D + c0) >> 1] : 0u;
-      qa[kk][1] = g + 8 < G ? q32[((g + 8) * D + c0) >> 1] : 0u;
-      qa[kk][2] = g < G ? q32[(g * D + c0 + 8) >> 1] : 0u;
-      qa[kk][3] = g + 8 < G ? q32[((g + 8) * D + c0 + 8) >> 1] : 0u;
-    }
-  }
-
   float o[D / 8][4];
-#pragma unroll
-  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  Unit un{};
+  int n_tok = 0, nsplit = 0;
 
-  bool ok = true;
-  for (int it = 0; it < n_iters; ++it) {
-    const int s = it % C::kStages;
-    const uint32_t ph = (it / C::kStages) & 1;
+  for (uint32_t it_g = 0;; ++it_g) {
+    const int s = it_g % C::kStages;
+    const uint32_t ph = (it_g / C::kStages) & 1;
     if (!ptx::mbar_wait(&full_bar[s], ph)) {
-      ok = false;
-      break;
+      report_timeout(p.status);
+      return;
     }
-    const int t_base = it * kStageTok + warp * 16;  // token of this warp's row 0, relative to split
+    const int4 md = meta[s];
+    if (md.x < 0) return;  // end of the work list
+    const int it = md.y;
+    if (it == 0) {
+      unit_of_ticket(p, md.x, un);
+      n_tok = md.z;
+      nsplit = md.w;
+      if (n_tok == 0) {
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&empty_bar[s]);
+        T* out = reinterpret_cast<T*>(p.out) + ((size_t)un.b * p.n_heads + un.kvh * G) * D;
+        for (int i = threadIdx.x; i < G * D; i += 128) out[i] = DT<T>::from_f(0.f);
+        continue;
+      }
+      // Q fragments (A operand, rows = query heads of this KV group, zero padded).
+      const uint32_t* q32 = reinterpret_cast<const uint32_t*>(qslot + s * q_bytes);
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const int c0 = kk * 16 + tig * 2;
+        qa[kk][0] = g < G ? q32[(g * D + c0) >> 1] : 0u;
+        qa[kk][1] = g + 8 < G ? q32[((g + 8) * D + c0) >> 1] : 0u;
+        qa[kk][2] = g < G ? q32[(g * D + c0 + 8) >> 1] : 0u;
+        qa[kk][3] = g + 8 < G ? q32[((g + 8) * D + c0 + 8) >> 1] : 0u;
+      }
+#pragma unroll
+      for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+      m0 = m1 = -INFINITY;
+      l0 = l1 = 0.f;
+    }
+
+    const int t_base = it * kStageTok + warp * 16;  // token of this warp's row 0, relative to the split
     if (t_base < n_tok) {
       const uint32_t kbase = base_u32 + s * C::kStageBytes;
       const uint32_t vbase = kbase + C::kKVBytes;
@@ -284,59 +490,56 @@ __global__ void __launch_bounds__(160, 2)
     }
     __syncwarp();
     if (lane == 0) ptx::mbar_arrive(&empty_bar[s]);
-  }
-  if (!ok) {
-    report_timeout(p.status);
-    return;
-  }
+    if ((it + 1) * kStageTok < n_tok) continue;
 
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-
-  // ---------------- combine the four warps through shared memory ----------
-  ptx::named_barrier_sync(1, 128);  // every consumer is done reading the ring
-  float* cm = reinterpret_cast<float*>(base);
-  float* cl = cm + 4 * kMaxGroup;
-  float* co = cl + 4 * kMaxGroup;
-  if (tig == 0) {
-    cm[warp * 16 + g] = m0;
-    cm[warp * 16 + g + 8] = m1;
-    cl[warp * 16 + g] = l0;
-    cl[warp * 16 + g + 8] = l1;
-  }
-#pragma unroll
-  for (int i = 0; i < D / 8; ++i) {
-    const int col = i * 8 + tig * 2;
-    co[(warp * 16 + g) * D + col] = o[i][0];
-    co[(warp * 16 + g) * D + col + 1] = o[i][1];
-    co[(warp * 16 + g + 8) * D + col] = o[i][2];
-    co[(warp * 16 + g + 8) * D + col + 1] = o[i][3];
-  }
-  ptx::named_barrier_sync(1, 128);
-
-  for (int idx = threadIdx.x; idx < G * D; idx += 128) {
-    const int r = idx / D, col = idx % D;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, cm[w * 16 + r]);
-    float L = 0.f, A = 0.f;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      const float e = exp2f(cm[w * 16 + r] - M);
-      L += cl[w * 16 + r] * e;
-      A += co[(w * 16 + r) * D + col] * e;
+    // ---------------- last stage of the unit: merge the four warps ----------
+    float L0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
+    L0 += __shfl_xor_sync(0xffffffffu, L0, 2);
+    float L1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
+    L1 += __shfl_xor_sync(0xffffffffu, L1, 2);
+    ptx::named_barrier_sync(1, 128);  // the previous unit's merge has been read
+    if (tig == 0) {
+      cm[warp * 16 + g] = m0;
+      cm[warp * 16 + g + 8] = m1;
+      cl[warp * 16 + g] = L0;
+      cl[warp * 16 + g + 8] = L1;
     }
-    const int h = kvh * G + r;
-    if (nsplit == 1) {
-      reinterpret_cast<T*>(p.out)[((size_t)b * p.n_heads + h) * D + col] = DT<T>::from_f(A / L);
-    } else {
-      const size_t row = ((size_t)b * p.n_heads + h) * p.max_splits + split;
-      p.part_o[row * D + col] = A;
-      if (col == 0) {
-        p.part_ml[row * 2] = M;
-        p.part_ml[row * 2 + 1] = L;
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      const int col = i * 8 + tig * 2;
+      if (g < G) {
+        co[(warp * G + g) * D + col] = o[i][0];
+        co[(warp * G + g) * D + col + 1] = o[i][1];
+      }
+      if (g + 8 < G) {
+        co[(warp * G + g + 8) * D + col] = o[i][2];
+        co[(warp * G + g + 8) * D + col + 1] = o[i][3];
+      }
+    }
+    ptx::named_barrier_sync(1, 128);
+
+    for (int idx = threadIdx.x; idx < G * D; idx += 128) {
+      const int r = idx / D, col = idx % D;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) M = fmaxf(M, cm[w * 16 + r]);
+      float L = 0.f, A = 0.f;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float e = exp2f(cm[w * 16 + r] - M);
+        L += cl[w * 16 + r] * e;
+        A += co[(w * G + r) * D + col] * e;
+      }
+      const int h = un.kvh * G + r;
+      if (nsplit == 1) {
+        reinterpret_cast<T*>(p.out)[((size_t)un.b * p.n_heads + h) * D + col] = DT<T>::from_f(A / L);
+      } else {
+        const size_t row = ((size_t)un.b * p.n_heads + h) * p.max_splits + un.split;
+        p.part_o[row * D + col] = A;
+        if (col == 0) {
+          p.part_ml[row * 2] = M;
+          p.part_ml[row * 2 + 1] = L;
+        }
       }
     }
   }
@@ -501,35 +704,68 @@ __global__ void __launch_bounds__(128) paged_decode_simt_kernel(const DecodePara
 // -----------------------------------------------------------------------------
 // split-K combine
 // -----------------------------------------------------------------------------
-template <typename T>
+// One CTA per (sequence, KV head); warp w merges query-head rows w, w+4, ...
+// The lanes first take 32 splits at a time for the max and the weights
+// exp2(m_i - M); then each lane owns D/32 output columns and adds the split
+// rows with the weights broadcast by shuffle, eight independent loads in
+// flight per lane.
+template <typename T, int D>
 __global__ void __launch_bounds__(128) paged_decode_combine_kernel(const DecodeParams p) {
   const int kvh = blockIdx.x, b = blockIdx.y;
   const int ctx = effective_ctx(p, b);
   if (ctx <= 0) return;
-  const int nsplit = (ctx + p.split_tokens - 1) / p.split_tokens;
+  const int split_tokens = p.device_split ? *reinterpret_cast<const int*>(p.sched + kSplitOffset) : p.split_tokens;
+  const int nsplit = (ctx + split_tokens - 1) / split_tokens;
   if (nsplit <= 1) return;
-  const int G = p.group, D = p.head_dim;
-  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
-    const int r = idx / D, col = idx % D;
+  const int G = p.group;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int per_lane = D / 32;  // 1, 2 or 4 columns
+  for (int r = warp; r < G; r += 4) {
     const int h = kvh * G + r;
     const size_t row0 = ((size_t)b * p.n_heads + h) * p.max_splits;
+    const float* ml = p.part_ml + row0 * 2;
+    const float* po = p.part_o + row0 * D;
     float M = -INFINITY;
-    for (int i = 0; i < nsplit; ++i) M = fmaxf(M, p.part_ml[(row0 + i) * 2]);
-    float L = 0.f, A = 0.f;
-    for (int i = 0; i < nsplit; ++i) {
-      const float e = exp2f(p.part_ml[(row0 + i) * 2] - M);
-      L += p.part_ml[(row0 + i) * 2 + 1] * e;
-      A += p.part_o[(row0 + i) * D + col] * e;
+    for (int i = lane; i < nsplit; i += 32) M = fmaxf(M, ml[i * 2]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    float L = 0.f;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c0 = 0; c0 < nsplit; c0 += 32) {
+      const int i = c0 + lane;
+      const float w = i < nsplit ? exp2f(ml[i * 2] - M) : 0.f;
+      L += i < nsplit ? ml[i * 2 + 1] * w : 0.f;
+      const int n = min(32, nsplit - c0);
+#pragma unroll 8
+      for (int j = 0; j < n; ++j) {
+        const float wj = __shfl_sync(0xffffffffu, w, j);
+        const float* src = po + (size_t)(c0 + j) * D + lane * per_lane;
+        if constexpr (per_lane == 4) {
+          const float4 v = *reinterpret_cast<const float4*>(src);
+          acc[0] += wj * v.x;
+          acc[1] += wj * v.y;
+          acc[2] += wj * v.z;
+          acc[3] += wj * v.w;
+        } else if constexpr (per_lane == 2) {
+          const float2 v = *reinterpret_cast<const float2*>(src);
+          acc[0] += wj * v.x;
+          acc[1] += wj * v.y;
+        } else {
+          acc[0] += wj * src[0];
+        }
+      }
     }
-    reinterpret_cast<T*>(p.out)[((size_t)b * p.n_heads + h) * D + col] = DT<T>::from_f(A / L);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    T* out = reinterpret_cast<T*>(p.out) + ((size_t)b * p.n_heads + h) * D + lane * per_lane;
+#pragma unroll
+    for (int k = 0; k < per_lane; ++k) out[k] = DT<T>::from_f(acc[k] / L);
   }
 }
 
 // -----------------------------------------------------------------------------
 // host side
 // -----------------------------------------------------------------------------
-constexpr int kTargetCtas = 148 * 3;  // about one and a half waves of 2 CTAs per SM
-
 int table_tokens(int block_size, int max_blocks, int max_context_len) {
   int blocks = max_blocks;
   if (max_context_len >= 0) {
@@ -539,14 +775,35 @@ int table_tokens(int block_size, int max_blocks, int max_context_len) {
   return blocks * block_size;
 }
 
-// Tokens per CTA: the largest of 512/256/128/64 that still gives enough CTAs
-// to fill the GPU when every sequence uses its whole table.  Larger splits mean
-// fewer partials to merge and fewer CTAs that find no live token.
-int choose_split(int batch, int n_kv_heads, int max_ctx_tokens) {
-  const long units = (long)batch * n_kv_heads;
-  for (int s = 512; s > kStageTok; s >>= 1)
-    if (units * ((max_ctx_tokens + s - 1) / s) >= kTargetCtas) return s;
+// Largest power of two in [64, max_split] that gives at least `target` units
+// when every sequence uses its whole table.
+int split_for(long bk, int table_tok, int max_split, long target) {
+  for (int s = max_split; s > kStageTok; s >>= 1)
+    if (bk * ((table_tok + s - 1) / s) >= target) return s;
   return kStageTok;
+}
+
+// How one call is cut into units and launched.
+//  * One CTA per unit (the simt kernel always; the tc kernel when that grid
+//    is at most two waves): units of up to 512 tokens, about 1.5 waves.
+//  * Otherwise persistent tc CTAs with the ticket counter: `split` is the
+//    smallest unit the kernel may use (it sizes the partials); the kernel
+//    picks the actual size from the live contexts.
+struct Plan {
+  int split, max_splits, dynamic;
+};
+
+Plan make_plan(int batch, int n_kv_heads, int table_tok, bool persistent_ok) {
+  const long bk = (long)batch * n_kv_heads;
+  Plan pl{};
+  pl.split = split_for(bk, table_tok, 512, kStaticTarget);
+  pl.max_splits = table_tok > 0 ? (table_tok + pl.split - 1) / pl.split : 1;
+  pl.dynamic = 0;
+  if (!persistent_ok || bk * pl.max_splits <= 2 * kSlots) return pl;
+  pl.split = split_for(bk, table_tok, kMaxSplitTokens, kTargetUnits);
+  pl.max_splits = table_tok > 0 ? (table_tok + pl.split - 1) / pl.split : 1;
+  pl.dynamic = 1;
+  return pl;
 }
 
 size_t workspace_bytes_for(int batch, int n_heads, int head_dim, int max_splits) {
@@ -584,15 +841,31 @@ int launch_tc(const DecodeParams& p, const void* k_cache, const void* v_cache, C
     return TVK_ERR_CUDA;
   }
   auto kern = paged_decode_tc_kernel<T, D, RB>;
+  const int smem = C::smem_bytes(p.group);
   static unsigned long long attr_set_mask = 0;  // per instantiation, one bit per device
+  static int ctas_per_sm[64][kMaxGroup + 1] = {};
+  static int num_sms[64] = {};
   int dev = 0;
   TVK_CHECK_CUDA(cudaGetDevice(&dev));
-  if (dev >= 64 || !(attr_set_mask & (1ull << dev))) {
-    TVK_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
-    if (dev < 64) attr_set_mask |= (1ull << dev);
+  if (dev >= 64) {
+    tvk::set_error("device index %d beyond 63", dev);
+    return TVK_ERR_UNSUPPORTED;
   }
-  dim3 grid(p.max_splits, p.n_kv_heads, p.batch);
-  kern<<<grid, 160, C::kSmemBytes, stream>>>(p, tmk, tmv);
+  if (!(attr_set_mask & (1ull << dev))) {
+    TVK_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::smem_bytes(kMaxGroup)));
+    TVK_CHECK_CUDA(cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev));
+    attr_set_mask |= (1ull << dev);
+  }
+  if (ctas_per_sm[dev][p.group] == 0) {
+    int n = 0;
+    TVK_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, 160, smem));
+    ctas_per_sm[dev][p.group] = n > 0 ? n : 1;
+  }
+  const long long units = (long long)p.batch * p.n_kv_heads * p.max_splits;
+  const long long slots = (long long)num_sms[dev] * ctas_per_sm[dev][p.group];
+  // Persistent grids fill the resident slots; otherwise one CTA per unit.
+  const int grid = (int)(p.dynamic && units > slots ? slots : units);
+  kern<<<grid, 160, smem, stream>>>(p, tmk, tmv);
   TVK_CHECK_LAUNCH("paged_decode_tc");
   return TVK_OK;
 }
@@ -619,7 +892,12 @@ int launch_typed(DecodeParams& p, bool use_tc, CUtensorMapDataType tdt, cudaStre
   }
   if (rc != TVK_OK) return rc;
   if (p.max_splits > 1) {
-    paged_decode_combine_kernel<T><<<dim3(p.n_kv_heads, p.batch), 128, 0, stream>>>(p);
+    const dim3 cgrid(p.n_kv_heads, p.batch);
+    switch (p.head_dim) {
+      case 32: paged_decode_combine_kernel<T, 32><<<cgrid, 128, 0, stream>>>(p); break;
+      case 64: paged_decode_combine_kernel<T, 64><<<cgrid, 128, 0, stream>>>(p); break;
+      default: paged_decode_combine_kernel<T, 128><<<cgrid, 128, 0, stream>>>(p); break;
+    }
     TVK_CHECK_LAUNCH("paged_decode_combine");
   }
   return TVK_OK;
@@ -631,10 +909,27 @@ extern "C" size_t tvk_paged_decode_workspace_size(int batch, int n_heads, int n_
                                                   int block_size, int max_blocks, int max_context_len) {
   if (batch <= 0 || n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || block_size <= 0 || max_blocks <= 0)
     return tvk::kWorkspaceHeader;
+  // The dtype is not known here: size for whichever plan needs more.
   const int tt = table_tokens(block_size, max_blocks, max_context_len);
-  const int split = choose_split(batch, n_kv_heads, tt);
-  const int max_splits = (tt + split - 1) / split;
-  return workspace_bytes_for(batch, n_heads, head_dim, max_splits);
+  const Plan a = make_plan(batch, n_kv_heads, tt, false);
+  const Plan b = make_plan(batch, n_kv_heads, tt, true);
+  return workspace_bytes_for(batch, n_heads, head_dim, a.max_splits > b.max_splits ? a.max_splits : b.max_splits);
+}
+
+extern "C" int tvk_paged_decode_plan(int batch, int n_heads, int n_kv_heads, int head_dim, int block_size,
+                                     int max_blocks, int max_context_len, int dtype, int* plan_out) {
+  TVK_CHECK_ARG(plan_out, "null plan_out");
+  TVK_CHECK_ARG(batch > 0 && n_heads > 0 && n_kv_heads > 0 && head_dim > 0 && block_size > 0 && max_blocks > 0,
+                "sizes must be positive");
+  const int tt = table_tokens(block_size, max_blocks, max_context_len);
+  const bool tc_shape = (dtype != TVK_DTYPE_F32) &&
+                        (block_size == 8 || block_size == 16 || block_size == 32 || block_size == 64);
+  const Plan pl = make_plan(batch, n_kv_heads, tt, tc_shape);
+  plan_out[0] = pl.split;
+  plan_out[1] = pl.max_splits;
+  plan_out[2] = pl.max_splits > 1 ? 2 : 1;
+  plan_out[3] = pl.dynamic;
+  return TVK_OK;
 }
 
 extern "C" int tvk_paged_decode_attention(const void* q, const void* k_cache, const void* v_cache,
@@ -650,6 +945,8 @@ extern "C" int tvk_paged_decode_attention(const void* q, const void* k_cache, co
   TVK_CHECK_ARG(n_heads / n_kv_heads <= kMaxGroup, "n_heads / n_kv_heads = %d exceeds %d", n_heads / n_kv_heads,
                 kMaxGroup);
   TVK_CHECK_ARG(batch <= 65535 && n_kv_heads <= 65535, "batch and n_kv_heads must be <= 65535");
+  TVK_CHECK_ARG((long long)batch * n_kv_heads * ((long long)max_blocks * block_size / 64 + 1) < 0x7fffffffLL,
+                "batch x KV heads x table splits exceeds the 32-bit work index");
   TVK_CHECK_ARG(block_size > 0 && num_blocks > 0 && max_blocks > 0,
                 "block_size, num_blocks and max_blocks must be positive");
   TVK_CHECK_ARG(dtype == TVK_DTYPE_F32 || dtype == TVK_DTYPE_F16 || dtype == TVK_DTYPE_BF16, "unknown dtype %d",
@@ -679,8 +976,11 @@ extern "C" int tvk_paged_decode_attention(const void* q, const void* k_cache, co
   p.num_blocks = num_blocks;
   p.max_blocks = max_blocks;
   p.max_ctx_tokens = table_tokens(block_size, max_blocks, max_context_len);
-  p.split_tokens = choose_split(batch, n_kv_heads, p.max_ctx_tokens);
-  p.max_splits = p.max_ctx_tokens > 0 ? (p.max_ctx_tokens + p.split_tokens - 1) / p.split_tokens : 1;
+  const bool tc_shape = (dtype != TVK_DTYPE_F32) &&
+                        (block_size == 8 || block_size == 16 || block_size == 32 || block_size == 64);
+  const Plan plan = make_plan(batch, n_kv_heads, p.max_ctx_tokens, tc_shape);
+  p.split_tokens = plan.split;
+  p.max_splits = plan.max_splits;
   p.scale_log2 = (float)(1.4426950408889634 / sqrt((double)head_dim));
 
   const size_t need = workspace_bytes_for(batch, n_heads, head_dim, p.max_splits);
@@ -693,12 +993,15 @@ extern "C" int tvk_paged_decode_attention(const void* q, const void* k_cache, co
   if (workspace) {
     TVK_CHECK_ARG((uintptr_t)workspace % 16 == 0, "workspace must be 16-byte aligned");
     p.status = reinterpret_cast<int*>(workspace);
+    p.sched = reinterpret_cast<uint8_t*>(workspace);
     float* f = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + tvk::kWorkspaceHeader);
     p.part_o = f;
     p.part_ml = f + (size_t)batch * n_heads * p.max_splits * head_dim;
   }
 
-  const bool tc_shape = (block_size == 8 || block_size == 16 || block_size == 32 || block_size == 64);
+  // The ticket counter and the device-side unit size need the header.
+  p.dynamic = (plan.dynamic && p.sched) ? 1 : 0;
+  p.device_split = p.dynamic;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   (void)es;
   switch (dtype) {
@@ -774,9 +1077,10 @@ extern "C" int tvk_paged_decode_attention_noalloc(const void* q, const void* k_c
   void* scratch = nullptr;
   const int rc = noalloc_scratch_ptr(&scratch);
   if (rc != TVK_OK) return rc;
-  // The scratch keeps the previous call's contents; only the status word has
-  // to start at zero (the split-K partials are written before they are read).
-  TVK_CHECK_CUDA(cudaMemsetAsync(scratch, 0, sizeof(int), reinterpret_cast<cudaStream_t>(stream)));
+  // The scratch keeps the previous call's contents; only the header (status
+  // word and work-list counters) has to start at zero (the split-K partials
+  // are written before they are read).
+  TVK_CHECK_CUDA(cudaMemsetAsync(scratch, 0, tvk::kWorkspaceHeader, reinterpret_cast<cudaStream_t>(stream)));
   return tvk_paged_decode_attention(q, k_cache, v_cache, block_tables, context_lens, out, batch, n_heads, n_kv_heads,
                                     head_dim, block_size, num_blocks, max_blocks, max_context_len, dtype, scratch,
                                     kNoAllocScratchBytes, stream);
