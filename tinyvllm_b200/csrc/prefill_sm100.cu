@@ -7,17 +7,19 @@
 // owns one 128-row query tile of one head of one prompt, walks only the key
 // tiles at or below the diagonal, and never leaves the chip with scores.
 //
-// tcgen05 kernel (fp16/bf16, head_dim 64 or 128), 6 warps:
-//   warp 0  TMA producer: Q once, then K/V 128-token tiles into a ring; for the
-//           diagonal tile (this CTA's own tokens) of the first query head of a
-//           KV group it also copies the landed K/V rows into their paged slots.
-//   warp 1  owns TMEM (512 columns) and issues the MMAs from one thread:
-//           S_j = Q.K_j^T (M=128, N=128, fp32 in TMEM, double buffered) and
-//           O_j = P_j.V_j (M=128, N=head_dim, fp32 in TMEM, double buffered).
-//   warps 2-5  softmax: one query row per thread, S read with tcgen05.ld,
-//           online softmax in the log2 domain, P written to shared memory in
-//           the 128-byte swizzled K-major layout, O_j folded into a register
-//           accumulator with the running rescale.
+// tcgen05 kernel (fp16/bf16, head_dim 64 or 128), 6 warps, persistent CTAs
+// walking a heaviest-first list of (prompt, 128-row query tile, head) items:
+//   warp 0  TMA producer: Q once per item, then 64-key K/V tiles into a ring;
+//           for the two diagonal tiles (this query tile's own tokens) of the
+//           first query head of a KV group it also copies the landed K/V rows
+//           into their paged slots.
+//   warp 1  owns TMEM and issues the MMAs from one thread: S(g) = Q.K(g)^T
+//           (M=128, N=64, fp32, two TMEM buffers), then O += P(g-1).V(g-1)
+//           (M=128, N=head_dim, A = P from TMEM, O in TMEM for the whole item),
+//           so the next tile's scores are computed while the softmax works.
+//   warps 2-5  softmax: one query row per thread, S read once with
+//           tcgen05.ld, online softmax in the log2 domain with a lazy O
+//           rescale, P packed to 16-bit pairs and stored to TMEM (two buffers).
 // SIMT kernel (any dtype incl. fp32, head_dim 32/64/128): one warp per four
 // query rows, fp32 CUDA-core math; also does the paged write.
 #include <math.h>
@@ -41,6 +43,7 @@ struct PrefillParams {
   int* status;                  // may be null
   const int32_t* sched;         // tc path: (seq << 16 | query tile) items, heaviest first
   const int32_t* sched_count;   // tc path: number of entries in sched
+  int* ticket;                  // tc path: next item to hand out (zeroed by the schedule kernel)
   int n_seqs, n_heads, n_kv_heads, group, head_dim, causal, num_blocks, block_size, n_mtiles;
   float scale_log2;
 };
@@ -80,31 +83,64 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// max(a, b, c) in one instruction (sm_100).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// (a0, a1) * b + c on the paired fp32 pipe: two results per instruction.
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b, float c) {
+  uint64_t A, B, Cc, Dd;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(A) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(B) : "f"(b));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(Cc) : "f"(c));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(Dd) : "l"(A), "l"(B), "l"(Cc));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(Dd));
+}
+
 template <int D>
 struct PfCfg {
-  static constexpr int kKB = D / 64;               // 64-element (128 B) column blocks per row
-  static constexpr int kBlockBytes = 128 * 128;    // one column block of a 128-row tile
-  static constexpr int kTileBytes = 128 * D * 2;   // one 128-row tile of Q, K or V
-  static constexpr int kStages = 3;                // K/V ring depth
-  static constexpr int kSBufs = D == 64 ? 1 : 2;   // S buffers in TMEM
+  static constexpr int kKB = D / 64;                  // 64-element (128 B) column blocks per row
+  static constexpr int kQBlockBytes = 128 * 128;      // one column block of the 128-row Q tile
+  static constexpr int kQBytes = 128 * D * 2;
+  static constexpr int kKvRows = 64;                  // keys per K/V tile
+  static constexpr int kKvBlockBytes = kKvRows * 128; // one column block of a 64-row K or V tile
+  static constexpr int kKvBytes = kKvRows * D * 2;
+  // P.V runs with N = head_dim + 16: the extra B columns are a block of ones,
+  // so O's column head_dim accumulates the row sum of P on the tensor cores.
+  // In the MN-major V operand the ones are one more 64-column block at the
+  // descriptor's block stride: after each stage's V tile at head_dim 128, one
+  // shared block after all stages at head_dim 64 (stride = its distance).
+  static constexpr int kVStageBytes = D == 128 ? kKvBytes + kKvBlockBytes : kKvBytes;
+  static constexpr int kStages = D == 64 ? 5 : 4;     // K/V ring depth (64-key tiles)
   static constexpr int kQOff = 0;
-  static constexpr int kKOff = kQOff + kTileBytes;
-  static constexpr int kVOff = kKOff + kStages * kTileBytes;
-  static constexpr int kBarOff = kVOff + kStages * kTileBytes;
-  // q_full, q_empty, k_full[S], v_full[S], kv_empty[S], s_full[SB], s_empty[SB], p_full, pv_done, o_empty, final
-  static constexpr int kNumBars = 2 + 3 * kStages + 2 * kSBufs + 4;
-  static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag
-  static constexpr int kUsed = kMiscOff + 16;
-  // head_dim 64: 113 KB so that two CTAs share an SM (2 x (113 + 1 reserved) KB = 228 KB);
-  // the slack above kUsed absorbs the 1024-byte alignment of the base.
+  static constexpr int kKOff = kQOff + kQBytes;
+  static constexpr int kVOff = kKOff + kStages * kKvBytes;
+  static constexpr int kOnesOff = kVOff + kStages * kVStageBytes;  // head_dim 64 only
+  static constexpr int kBarOff = kOnesOff + (D == 64 ? kKvBlockBytes : 0);
+  // q_full, q_empty, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2], pv_done[2], o_empty, final,
+  // item_full[4], item_empty[4]
+  static constexpr int kItemSlots = 4;
+  static constexpr int kNumBars = 2 + 3 * kStages + 6 + 2 + 2 * kItemSlots;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag, item ring
+  static constexpr int kUsed = kMiscOff + 16 + 4 * kItemSlots;
+  // head_dim 64: at most 113 KB so that two CTAs share an SM
+  // (2 x (113 + 1 reserved) KB = 228 KB); the slack above kUsed absorbs the
+  // 1024-byte alignment of the base.
   static constexpr int kCtasPerSm = D == 64 ? 2 : 1;
-  static constexpr int kSmemBytes = D == 64 ? 115712 : kUsed + 1024;
-  // TMEM columns: S buffers, then the O accumulator, then P (128 keys as 64
-  // columns of packed 16-bit pairs, the A operand of P.V)
-  static constexpr uint32_t kOCol = kSBufs * 128;
-  static constexpr uint32_t kPCol = kOCol + D;
-  static constexpr uint32_t kTmemCols = kPCol + 64 <= 256 ? 256 : 512;
-  static_assert(kUsed <= kSmemBytes, "shared memory layout overflows");
+  static constexpr int kSmemBytes = kUsed + 1024;
+  static_assert(D != 64 || kSmemBytes <= 115712, "two CTAs per SM at head_dim 64");
+  static_assert(kSmemBytes <= 232448, "shared memory per CTA");
+  // TMEM columns: two S buffers of 64 fp32 columns (64 keys); once a tile's
+  // scores are in registers its P (64 keys as 32 columns of packed 16-bit
+  // pairs, the A operand of P.V) is written over the first half of the same
+  // buffer.  Then O: head_dim columns plus the row-sum column (and 15 unused).
+  static constexpr uint32_t kSCol = 0;
+  static constexpr uint32_t kOCol = 128;
+  static constexpr int kOCols = D + 16;
+  static constexpr uint32_t kTmemCols = kOCol + kOCols <= 256 ? 256 : 512;
 };
 
 // One unit of work: a 128-row query tile of one head of one prompt.
@@ -112,20 +148,20 @@ struct Item {
   int seq, mtile, h, s0, L;
 };
 
-// Round k of this CTA's work: item w = k*G + i (k even) or k*G + G-1-i (k odd)
-// of the schedule (query tiles sorted heaviest first, each expanded over the
-// query heads).  The snake order balances the heavy early items with light
-// late ones across CTAs.
-__device__ __forceinline__ bool next_item(const PrefillParams& p, int n_items, int& k, Item& it) {
-  const int G = gridDim.x, i = blockIdx.x;
-  const int w = k * G + ((k & 1) ? (G - 1 - i) : i);
-  if (w >= n_items) return false;
+// Item w of the schedule: query tiles sorted heaviest first, each expanded
+// over the query heads.  CTAs take items from the ticket counter as they free
+// up, so the heavy items start first and the light ones fill the gaps.
+__device__ __forceinline__ Item item_of(const PrefillParams& p, int w) {
   const int e = __ldg(p.sched + w / p.n_heads);
   const int seq = e >> 16, m = e & 0xFFFF;
   const int s0 = __ldg(p.cu_seqlens + seq);
-  it = Item{seq, m, w % p.n_heads, s0, __ldg(p.cu_seqlens + seq + 1) - s0};
-  ++k;
-  return true;
+  return Item{seq, m, w % p.n_heads, s0, __ldg(p.cu_seqlens + seq + 1) - s0};
+}
+
+// 64-key tiles an item visits: up to and including the diagonal when causal.
+__device__ __forceinline__ int kv_tiles(const PrefillParams& p, const Item& it) {
+  const int all = (it.L + 63) / 64;
+  return p.causal ? min(2 * it.mtile + 2, all) : all;
 }
 
 template <typename T, int D>
@@ -133,13 +169,13 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
     flash_prefill_tc_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tm_q,
                             const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
   using C = PfCfg<D>;
-  constexpr int S = C::kStages, SB = C::kSBufs;
+  constexpr int S = C::kStages;
   constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = ptx::smem_u32(smem_raw);
   const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
-  if (base_u32 + C::kUsed > raw_u32 + C::kSmemBytes) {  // cannot happen with a >=128 B aligned base
+  if (base_u32 + C::kUsed > raw_u32 + C::kSmemBytes) {  // cannot happen with a >=16 B aligned base
     if (threadIdx.x == 0) report(p.status);
     return;
   }
@@ -150,13 +186,15 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
   uint64_t* v_full = k_full + S;
   uint64_t* kv_empty = v_full + S;
   uint64_t* s_full = kv_empty + S;
-  uint64_t* s_empty = s_full + SB;
-  uint64_t* p_full = s_empty + SB;
-  uint64_t* pv_done = p_full + 1;
-  uint64_t* o_empty = pv_done + 1;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* pv_done = p_full + 2;
+  uint64_t* o_empty = pv_done + 2;
   uint64_t* final_bar = o_empty + 1;
+  uint64_t* item_full = final_bar + 1;
+  uint64_t* item_empty = item_full + C::kItemSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + C::kMiscOff + 4);
+  volatile int* item_ring = reinterpret_cast<volatile int*>(base + C::kMiscOff + 16);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 1) {
@@ -171,22 +209,49 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
       ptx::mbar_init(&v_full[s], 1);
       ptx::mbar_init(&kv_empty[s], 1);
     }
-    for (int b = 0; b < SB; ++b) {
+    for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(&s_full[b], 1);
-      ptx::mbar_init(&s_empty[b], 4);
+      ptx::mbar_init(&p_full[b], 4);
+      ptx::mbar_init(&pv_done[b], 1);
     }
-    ptx::mbar_init(p_full, 4);
-    ptx::mbar_init(pv_done, 1);
     ptx::mbar_init(o_empty, 4);
     ptx::mbar_init(final_bar, 1);
+    for (int i = 0; i < C::kItemSlots; ++i) {
+      ptx::mbar_init(&item_full[i], 1);
+      ptx::mbar_init(&item_empty[i], 5);  // the MMA thread and the four softmax warps
+    }
     *abort_flag = 0;
     ptx::fence_mbar_init();
+  }
+  {
+    // the ones block(s) of the row-sum columns, read by the tensor cores
+    const uint32_t one2 = std::is_same<T, __half>::value ? 0x3C003C00u : 0x3F803F80u;
+    constexpr int kOnesBlocks = D == 64 ? 1 : S;
+    for (int i = threadIdx.x; i < kOnesBlocks * C::kKvBlockBytes / 16; i += blockDim.x) {
+      const int blk = i / (C::kKvBlockBytes / 16), w = i % (C::kKvBlockBytes / 16);
+      const int off = D == 64 ? C::kOnesOff : C::kVOff + blk * C::kVStageBytes + C::kKvBytes;
+      reinterpret_cast<uint4*>(base + off)[w] = make_uint4(one2, one2, one2, one2);
+    }
+    umma::fence_proxy_async_smem();
   }
   umma::fence_before_sync();
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
   const int n_items = __ldg(p.sched_count) * p.n_heads;
+  // Items reach the MMA and softmax warps through a small ring that the
+  // producer fills from the ticket counter; -1 ends the list.
+  uint32_t n_seen = 0;
+  auto take_item = [&](Item& it, bool arrive) -> int {  // 1: item, 0: end of list, -1: gave up
+    const int slot = n_seen % C::kItemSlots;
+    if (!wait_or_abort(&item_full[slot], (n_seen / C::kItemSlots) & 1, abort_flag)) return -1;
+    const int w = item_ring[slot];
+    if (arrive) ptx::mbar_arrive(&item_empty[slot]);
+    ++n_seen;
+    if (w < 0) return 0;
+    it = item_of(p, w);
+    return 1;
+  };
 
   if (warp == 0) {
     // =========================== TMA producer ===============================
@@ -197,17 +262,32 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
       ptx::prefetch_tmap(&tm_k);
       ptx::prefetch_tmap(&tm_v);
     }
-    int k = 0;
+    const long long n_slots = (long long)p.num_blocks * p.block_size;
+    uint32_t n_claim = 0;
     Item it;
-    while (ok && next_item(p, n_items, k, it)) {
-      const int n_kv = p.causal ? it.mtile + 1 : (it.L + 127) / 128;
+    while (ok) {
+      const int slot = n_claim % C::kItemSlots;
+      int w = 0;
+      if (lane == 0) w = (int)atomicAdd(p.ticket, 1);
+      w = __shfl_sync(0xffffffffu, w, 0);
+      if (w >= n_items) w = -1;
+      ok = __all_sync(0xffffffffu, wait_or_abort(&item_empty[slot], ((n_claim / C::kItemSlots) & 1) ^ 1, abort_flag));
+      if (!ok) break;
+      if (lane == 0) {
+        item_ring[slot] = w;
+        ptx::mbar_arrive(&item_full[slot]);
+      }
+      ++n_claim;
+      if (w < 0) break;
+      it = item_of(p, w);
+      const int n_kv = kv_tiles(p, it);
       const int kvh = it.h / p.group;
       ok = __all_sync(0xffffffffu, wait_or_abort(q_empty, (q_it & 1) ^ 1, abort_flag));
       if (!ok) break;
       if (lane == 0) {
-        ptx::mbar_arrive_expect_tx(q_full, C::kTileBytes);
+        ptx::mbar_arrive_expect_tx(q_full, C::kQBytes);
         for (int kb = 0; kb < C::kKB; ++kb)
-          tma_load_3d(base + C::kQOff + kb * C::kBlockBytes, &tm_q, q_full, kb * 64, it.h, it.s0 + it.mtile * 128);
+          tma_load_3d(base + C::kQOff + kb * C::kQBlockBytes, &tm_q, q_full, kb * 64, it.h, it.s0 + it.mtile * 128);
       }
       ++q_it;
       const bool write_kv = p.slot_mapping != nullptr && (it.h % p.group) == 0;
@@ -216,31 +296,36 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
         const uint32_t ph = (kv_it / S) & 1;
         ok = __all_sync(0xffffffffu, wait_or_abort(&kv_empty[st], ph ^ 1, abort_flag));
         if (!ok) break;
-        uint8_t* ks = base + C::kKOff + st * C::kTileBytes;
-        uint8_t* vs = base + C::kVOff + st * C::kTileBytes;
+        uint8_t* ks = base + C::kKOff + st * C::kKvBytes;
+        uint8_t* vs = base + C::kVOff + st * C::kVStageBytes;
         if (lane == 0) {
-          ptx::mbar_arrive_expect_tx(&k_full[st], C::kTileBytes);
+          ptx::mbar_arrive_expect_tx(&k_full[st], C::kKvBytes);
           for (int kb = 0; kb < C::kKB; ++kb)
-            tma_load_3d(ks + kb * C::kBlockBytes, &tm_k, &k_full[st], kb * 64, kvh, it.s0 + j * 128);
-          ptx::mbar_arrive_expect_tx(&v_full[st], C::kTileBytes);
+            tma_load_3d(ks + kb * C::kKvBlockBytes, &tm_k, &k_full[st], kb * 64, kvh, it.s0 + j * 64);
+          ptx::mbar_arrive_expect_tx(&v_full[st], C::kKvBytes);
           for (int kb = 0; kb < C::kKB; ++kb)
-            tma_load_3d(vs + kb * C::kBlockBytes, &tm_v, &v_full[st], kb * 64, kvh, it.s0 + j * 128);
+            tma_load_3d(vs + kb * C::kKvBlockBytes, &tm_v, &v_full[st], kb * 64, kvh, it.s0 + j * 64);
         }
-        if (write_kv && j == it.mtile) {
-          // The diagonal tile holds exactly this query tile's own tokens: copy the
-          // landed rows into their paged slots (slot = block * block_size + offset).
+        if (write_kv && (j >> 1) == it.mtile) {
+          // The two diagonal tiles hold exactly this query tile's own tokens: copy
+          // the landed rows into their paged slots (slot = block * block_size + offset).
           ok = __all_sync(0xffffffffu, wait_or_abort(&k_full[st], ph, abort_flag) &&
                                            wait_or_abort(&v_full[st], ph, abort_flag));
           if (!ok) break;
-          const int rows = min(128, it.L - it.mtile * 128);
-          const long long n_slots = (long long)p.num_blocks * p.block_size;
+          const int tok0 = it.s0 + j * 64, rows = min(64, it.L - j * 64);
           T* kc = reinterpret_cast<T*>(p.k_cache);
           T* vc = reinterpret_cast<T*>(p.v_cache);
-          for (int i = lane; i < rows * (D / 8); i += 32) {
+          // one slot per lane for rows lane and lane + 32, shared by shuffles
+          const long long slot_lo = lane < rows ? p.slot_mapping[tok0 + lane] : -1;
+          const long long slot_hi = lane + 32 < rows ? p.slot_mapping[tok0 + lane + 32] : -1;
+          for (int i0 = 0; i0 < rows * (D / 8); i0 += 32) {
+            const int i = i0 + lane;
             const int r = i / (D / 8), c8 = i % (D / 8);
-            const long long slot = p.slot_mapping[it.s0 + it.mtile * 128 + r];
-            if (slot < 0 || slot >= n_slots) continue;
-            const uint32_t off = (c8 / 8) * C::kBlockBytes + r * 128 + ((((c8 & 7) ^ (r & 7))) << 4);
+            const long long a = __shfl_sync(0xffffffffu, slot_lo, r & 31);
+            const long long b = __shfl_sync(0xffffffffu, slot_hi, r & 31);
+            const long long slot = r < 32 ? a : b;
+            if (i >= rows * (D / 8) || slot < 0 || slot >= n_slots) continue;
+            const uint32_t off = (c8 / 8) * C::kKvBlockBytes + r * 128 + ((((c8 & 7) ^ (r & 7))) << 4);
             const size_t dst = ((size_t)slot * p.n_kv_heads + kvh) * D + c8 * 8;
             *reinterpret_cast<uint4*>(kc + dst) = *reinterpret_cast<const uint4*>(ks + off);
             *reinterpret_cast<uint4*>(vc + dst) = *reinterpret_cast<const uint4*>(vs + off);
@@ -259,61 +344,67 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
     }
   } else if (warp == 1) {
     // =========================== MMA issuer =================================
+    // Order per tile g: S(g) = Q.K(g)^T into TMEM buffer g%2, then O += P(g-1).V(g-1),
+    // so the next tile's scores are computed while the softmax works on this one.
+    // Buffer g%2 holds P(g-2) until that P.V completes, so S(g) waits for it.
     if (lane == 0) {
-      const uint32_t idesc_s = umma::idesc_f16(128, 128, kBf16, false);
-      const uint32_t idesc_o = umma::idesc_f16(128, D, kBf16, true);
+      const uint32_t idesc_s = umma::idesc_f16(128, 64, kBf16, false);
+      const uint32_t idesc_o = umma::idesc_f16(128, C::kOCols, kBf16, true);
       const uint32_t q_addr = base_u32 + C::kQOff;
-      uint32_t kv_it = 0, q_it = 0, s_it = 0, pv_it = 0, item_it = 0;
+      uint32_t g = 0, q_it = 0, item_it = 0;
       bool ok = true;
-      int k = 0;
       Item it;
-      while (ok && next_item(p, n_items, k, it)) {
-        const int n_kv = p.causal ? it.mtile + 1 : (it.L + 127) / 128;
-        const uint32_t kv_base = kv_it;
-        auto issue_pv = [&](int i) -> bool {
-          const uint32_t g = kv_base + i;
-          const int st = g % S;
-          if (!wait_or_abort(p_full, pv_it & 1, abort_flag)) return false;
-          if (i == 0 && !wait_or_abort(o_empty, (item_it & 1) ^ 1, abort_flag)) return false;
-          if (!wait_or_abort(&v_full[st], (g / S) & 1, abort_flag)) return false;
-          umma::fence_after_sync();
-          const uint32_t v_addr = base_u32 + C::kVOff + st * C::kTileBytes;
+      auto issue_pv = [&](uint32_t gg, bool first) -> bool {
+        const int st = gg % S;
+        const int pb = gg & 1;
+        if (!wait_or_abort(&p_full[pb], (gg >> 1) & 1, abort_flag)) return false;
+        if (first && !wait_or_abort(o_empty, (item_it & 1) ^ 1, abort_flag)) return false;
+        if (!wait_or_abort(&v_full[st], (gg / S) & 1, abort_flag)) return false;
+        umma::fence_after_sync();
+        const uint32_t v_addr = base_u32 + C::kVOff + st * C::kVStageBytes;
+        const uint32_t lbo = D == 64 ? (uint32_t)(C::kOnesOff - (C::kVOff + st * C::kVStageBytes)) : C::kKvBlockBytes;
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {  // 16 keys per MMA: 8 TMEM columns of P
-            const uint64_t bd = umma::smem_desc_sw128(v_addr + ks * 2048, C::kBlockBytes, 1024);
-            umma::mma_f16_ts(tmem + C::kOCol, tmem + C::kPCol + ks * 8, bd, idesc_o, (i > 0 || ks > 0) ? 1u : 0u);
-          }
-          umma::commit(pv_done);
-          umma::commit(&kv_empty[st]);
-          ++pv_it;
-          return true;
-        };
+        for (int ks = 0; ks < 4; ++ks) {  // 16 keys per MMA: 8 TMEM columns of P
+          const uint64_t bd = umma::smem_desc_sw128(v_addr + ks * 2048, lbo, 1024);
+          umma::mma_f16_ts(tmem + C::kOCol, tmem + C::kSCol + pb * 64 + ks * 8, bd, idesc_o,
+                           (first && ks == 0) ? 0u : 1u);
+        }
+        umma::commit(&pv_done[pb]);
+        umma::commit(&kv_empty[st]);
+        return true;
+      };
+      while (ok) {
+        const int got = take_item(it, true);
+        if (got <= 0) {
+          ok = got == 0;
+          break;
+        }
+        const int n_kv = kv_tiles(p, it);
         ok = wait_or_abort(q_full, q_it & 1, abort_flag);
-        for (int j = 0; ok && j < n_kv; ++j) {
-          const uint32_t g = kv_base + j;
+        for (int j = 0; ok && j < n_kv; ++j, ++g) {
           const int st = g % S;
-          const int sb = s_it % SB;
+          const int sb = g & 1;
           ok = wait_or_abort(&k_full[st], (g / S) & 1, abort_flag) &&
-               wait_or_abort(&s_empty[sb], ((s_it / SB) & 1) ^ 1, abort_flag);
+               wait_or_abort(&pv_done[sb], ((g >> 1) & 1) ^ 1, abort_flag);
           if (!ok) break;
           umma::fence_after_sync();
-          const uint32_t k_addr = base_u32 + C::kKOff + st * C::kTileBytes;
+          const uint32_t k_addr = base_u32 + C::kKOff + st * C::kKvBytes;
 #pragma unroll
           for (int ks = 0; ks < D / 16; ++ks) {
-            const uint64_t ad = umma::smem_desc_sw128(q_addr + (ks >> 2) * C::kBlockBytes + (ks & 3) * 32, 16, 1024);
-            const uint64_t bd = umma::smem_desc_sw128(k_addr + (ks >> 2) * C::kBlockBytes + (ks & 3) * 32, 16, 1024);
-            umma::mma_f16_ss(tmem + sb * 128, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
+            const uint64_t ad =
+                umma::smem_desc_sw128(q_addr + (ks >> 2) * C::kQBlockBytes + (ks & 3) * 32, 16, 1024);
+            const uint64_t bd =
+                umma::smem_desc_sw128(k_addr + (ks >> 2) * C::kKvBlockBytes + (ks & 3) * 32, 16, 1024);
+            umma::mma_f16_ss(tmem + C::kSCol + sb * 64, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
           }
           umma::commit(&s_full[sb]);
-          ++s_it;
           if (j == n_kv - 1) umma::commit(q_empty);  // Q is free once this item's S MMAs are done
-          if (j >= 1) ok = issue_pv(j - 1);
+          if (j >= 1) ok = issue_pv(g - 1, j == 1);
         }
-        if (ok) ok = issue_pv(n_kv - 1);
-        kv_it += n_kv;
+        if (ok) ok = issue_pv(g - 1, n_kv == 1);
         ++q_it;
         ++item_it;
-        }
+      }
       if (!ok) report(p.status);
       // Drain: every MMA issued so far completes before TMEM is released.
       umma::commit(final_bar);
@@ -326,56 +417,62 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
     const int r = quarter * 32 + lane;
     const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
     const float sl2 = p.scale_log2;
-    uint32_t s_it = 0, pv_it = 0;
+    uint32_t g = 0;  // K/V tiles seen by this CTA (S, P and P.V buffers follow it)
     bool ok = true;
-    int k = 0;
     Item it;
-    while (ok && next_item(p, n_items, k, it)) {
-      const int n_kv = p.causal ? it.mtile + 1 : (it.L + 127) / 128;
+    // wait until O += P(gg).V(gg) has completed
+    auto wait_pv = [&](uint32_t gg) -> bool {
+      return __all_sync(0xffffffffu, wait_or_abort(&pv_done[gg & 1], (gg >> 1) & 1, abort_flag));
+    };
+    while (ok) {
+      int got = take_item(it, false);
+      ok = __all_sync(0xffffffffu, got >= 0);
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&item_empty[(n_seen - 1) % C::kItemSlots]);
+      if (got == 0) break;
+      const int n_kv = kv_tiles(p, it);
       const int q_pos = it.mtile * 128 + r;
       const int lim = p.causal ? min(q_pos + 1, it.L) : it.L;  // keys [0, lim) are visible
       float m = -INFINITY;  // running max (log2 domain) that P and O are scaled by
-      float l = 0.f;
-      for (int j = 0; j < n_kv; ++j) {
-        const int sb = s_it % SB;
-        ok = __all_sync(0xffffffffu, wait_or_abort(&s_full[sb], (s_it / SB) & 1, abort_flag));
+      for (int j = 0; j < n_kv; ++j, ++g) {
+        const int sb = g & 1;
+        ok = __all_sync(0xffffffffu, wait_or_abort(&s_full[sb], (g >> 1) & 1, abort_flag));
         if (!ok) break;
         umma::fence_after_sync();
-        const int lim_rel = lim - j * 128;  // keys [0, lim_rel) of this tile are visible
-        const uint32_t s_addr = t_lane + sb * 128;
-        // pass 1: row max of the visible raw scores (two 64-column loads per wait)
-        float mx = -INFINITY;
+        float s[64];
+        umma::ld_32x32b_x32(t_lane + C::kSCol + sb * 64, *reinterpret_cast<float(*)[32]>(&s[0]));
+        umma::ld_32x32b_x32(t_lane + C::kSCol + sb * 64 + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
+        umma::ld_wait();
+
+        const int lim_rel = lim - j * 64;  // keys [0, lim_rel) of this tile are visible
+        if (__any_sync(0xffffffffu, lim_rel < 64)) {
 #pragma unroll
-        for (int c = 0; c < 4; c += 2) {
-          float s[64];
-          umma::ld_32x32b_x32(s_addr + c * 32, *reinterpret_cast<float(*)[32]>(&s[0]));
-          umma::ld_32x32b_x32(s_addr + c * 32 + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
-          umma::ld_wait();
-          if (lim_rel >= 128) {
-#pragma unroll
-            for (int x = 0; x < 64; ++x) mx = fmaxf(mx, s[x]);
-          } else {
-#pragma unroll
-            for (int x = 0; x < 64; ++x) mx = fmaxf(mx, c * 32 + x < lim_rel ? s[x] : -INFINITY);
-          }
+          for (int x = 0; x < 64; ++x) s[x] = x < lim_rel ? s[x] : -INFINITY;
         }
+        // row max: eight independent partial maxima, three inputs per instruction
+        float mp[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          mp[i] = max3f(s[i], s[8 + i], s[16 + i]);
+          mp[i] = max3f(mp[i], s[24 + i], s[32 + i]);
+          mp[i] = max3f(mp[i], s[40 + i], s[48 + i]);
+          mp[i] = fmaxf(mp[i], s[56 + i]);
+        }
+        const float mx = max3f(max3f(mp[0], mp[1], mp[2]), max3f(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
         float m_cand = fmaxf(m, mx * sl2);
         if (m_cand == -INFINITY) m_cand = 0.f;  // no visible key (cannot happen for a live tile)
-        // P is single-buffered and O is rescaled in place, so the previous P.V must be
-        // complete before either is touched; wait for it as late as possible.
-        bool pv_waited = (j == 0);
         if (j == 0) {
           m = m_cand;
         } else if (__any_sync(0xffffffffu, m_cand > m + 8.f)) {
           // Lazy rescale: the stale max is kept unless the new one is 2^8 larger.
-          ok = __all_sync(0xffffffffu, wait_or_abort(pv_done, pv_it & 1, abort_flag));
+          // O is stable once the previous tile's P.V is done (this tile's needs P).
+          ok = wait_pv(g - 1);
           if (!ok) break;
-          ++pv_it;
-          pv_waited = true;
           umma::fence_after_sync();
           const float corr = ex2(m - m_cand);
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < (C::kOCols + 31) / 32; ++c) {  // O and its row-sum column
             float o[32];
             umma::ld_32x32b_x32(t_lane + C::kOCol + c * 32, o);
             umma::ld_wait();
@@ -384,55 +481,38 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
             umma::st_32x32b_x32(t_lane + C::kOCol + c * 32, o);
           }
           umma::st_wait();
-          l *= corr;
           m = m_cand;
         }
-        // P (TMEM, single-buffered) is still the A operand of the previous P.V until it completes
-        if (!pv_waited) {
-          ok = __all_sync(0xffffffffu, wait_or_abort(pv_done, pv_it & 1, abort_flag));
-          if (!ok) break;
-          ++pv_it;
+        // P = 2^(s*scale - m), packed to 16-bit pairs (row r = lane, 32 columns
+        // for 64 keys): the A operand of P.V
+        // (the row sum comes from the ones column of P.V)
+        uint32_t pk[32];
+#pragma unroll
+        for (int x = 0; x < 32; ++x) {
+          float x0, x1;
+          fma2(x0, x1, s[2 * x], s[2 * x + 1], sl2, -m);
+          pk[x] = DT<T>::pack2(ex2(x0), ex2(x1));
         }
-        // pass 2: P = 2^(s*scale - m), packed to fp16/bf16 pairs and stored to TMEM
-        // (row r = lane, 64 columns for 128 keys): the A operand of P.V
-        float sum = 0.f;
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          float s[64];
-          umma::ld_32x32b_x32(s_addr + hf * 64, *reinterpret_cast<float(*)[32]>(&s[0]));
-          umma::ld_32x32b_x32(s_addr + hf * 64 + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
-          umma::ld_wait();
-          if (lim_rel < 128) {
-#pragma unroll
-            for (int x = 0; x < 64; ++x) s[x] = hf * 64 + x < lim_rel ? s[x] : -INFINITY;
-          }
-          uint32_t pk[32];
-#pragma unroll
-          for (int x = 0; x < 32; ++x) {
-            const float p0 = ex2(fmaf(s[2 * x], sl2, -m));
-            const float p1 = ex2(fmaf(s[2 * x + 1], sl2, -m));
-            sum += p0 + p1;
-            pk[x] = DT<T>::pack2(p0, p1);
-          }
-          umma::st_32x32b_x32_u(t_lane + C::kPCol + hf * 32, pk);
-        }
+        // P(g) overwrites the scores of tile g; S(g) has been read and the P.V of
+        // tile g-2, the buffer's previous P, completed before S(g) was issued.
+        umma::st_32x32b_x32_u(t_lane + C::kSCol + sb * 64, pk);
         umma::st_wait();
-        // S has been read: hand the TMEM buffer back to the MMA warp.
         umma::fence_before_sync();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&s_empty[sb]);
-        ++s_it;
-        l += sum;
-        umma::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(p_full);
+        if (lane == 0) ptx::mbar_arrive(&p_full[sb]);
       }
       if (!ok) break;
       // ---- item done: O (TMEM) / l -> out
-      ok = __all_sync(0xffffffffu, wait_or_abort(pv_done, pv_it & 1, abort_flag));
+      ok = wait_pv(g - 1);
       if (!ok) break;
-      ++pv_it;
       umma::fence_after_sync();
+      float l;
+      {
+        float o[32];
+        umma::ld_32x32b_x32(t_lane + C::kOCol + D, o);
+        umma::ld_wait();
+        l = o[0];
+      }
       const float inv = l > 0.f ? 1.f / l : 0.f;
       T* orow = reinterpret_cast<T*>(p.out) + ((size_t)(it.s0 + q_pos) * p.n_heads + it.h) * D;
 #pragma unroll
@@ -567,8 +647,9 @@ constexpr int kMaxBands = 4096;  // query tiles per prompt: max_seqlen <= 524288
 
 __global__ void __launch_bounds__(1024) prefill_schedule_kernel(const int32_t* __restrict__ cu, int n_seqs,
                                                                 int n_bands, int capacity, int32_t* sched,
-                                                                int32_t* count, int* status) {
+                                                                int32_t* count, int* ticket, int* status) {
   __shared__ int band[kMaxBands];
+  if (threadIdx.x == 0) *ticket = 0;
   for (int m = threadIdx.x; m < n_bands; m += blockDim.x) band[m] = 0;
   __syncthreads();
   for (int s = threadIdx.x; s < n_seqs; s += blockDim.x) {
@@ -599,7 +680,8 @@ __global__ void __launch_bounds__(1024) prefill_schedule_kernel(const int32_t* _
 // -----------------------------------------------------------------------------
 // host side
 // -----------------------------------------------------------------------------
-int encode_rows_map(CUtensorMap* m, const void* ptr, CUtensorMapDataType tdt, int D, int heads, int total) {
+int encode_rows_map(CUtensorMap* m, const void* ptr, CUtensorMapDataType tdt, int D, int heads, int total,
+                    int box_rows) {
   tvk::EncodeTiledFn encode = tvk::encode_tiled_fn();
   if (!encode) {
     tvk::set_error("cuTensorMapEncodeTiled is not available from the driver");
@@ -607,7 +689,7 @@ int encode_rows_map(CUtensorMap* m, const void* ptr, CUtensorMapDataType tdt, in
   }
   cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)heads, (cuuint64_t)total};
   cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)heads * D * 2};
-  cuuint32_t box[3] = {64u, 1u, 128u};
+  cuuint32_t box[3] = {64u, 1u, (cuuint32_t)box_rows};
   cuuint32_t estr[3] = {1u, 1u, 1u};
   CUresult r = encode(m, tdt, 3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -622,14 +704,14 @@ template <typename T, int D>
 int launch_tc(const PrefillParams& p, int total, int sched_capacity, CUtensorMapDataType tdt, cudaStream_t stream) {
   using C = PfCfg<D>;
   CUtensorMap tq, tk, tv;
-  int rc = encode_rows_map(&tq, p.q, tdt, D, p.n_heads, total);
-  if (rc == TVK_OK) rc = encode_rows_map(&tk, p.k, tdt, D, p.n_kv_heads, total);
-  if (rc == TVK_OK) rc = encode_rows_map(&tv, p.v, tdt, D, p.n_kv_heads, total);
+  int rc = encode_rows_map(&tq, p.q, tdt, D, p.n_heads, total, 128);
+  if (rc == TVK_OK) rc = encode_rows_map(&tk, p.k, tdt, D, p.n_kv_heads, total, C::kKvRows);
+  if (rc == TVK_OK) rc = encode_rows_map(&tv, p.v, tdt, D, p.n_kv_heads, total, C::kKvRows);
   if (rc != TVK_OK) return rc;
   auto kern = flash_prefill_tc_kernel<T, D>;
   prefill_schedule_kernel<<<1, 1024, 0, stream>>>(p.cu_seqlens, p.n_seqs, p.n_mtiles, sched_capacity,
                                                   const_cast<int32_t*>(p.sched), const_cast<int32_t*>(p.sched_count),
-                                                  p.status);
+                                                  p.ticket, p.status);
   TVK_CHECK_LAUNCH("prefill_schedule");
   static unsigned long long attr_mask = 0;
   int dev = 0;
@@ -731,6 +813,7 @@ extern "C" int tvk_flash_prefill_attention(const void* q, const void* k, const v
     TVK_CHECK_ARG((uintptr_t)workspace % 16 == 0, "workspace must be 16-byte aligned");
     int32_t* w32 = reinterpret_cast<int32_t*>(workspace);
     p.sched_count = w32 + 1;
+    p.ticket = w32 + 2;
     p.sched = w32 + tvk::kWorkspaceHeader / 4;
     const int cap = (int)((need - tvk::kWorkspaceHeader) / 4);
     if (dtype == TVK_DTYPE_F16)
