@@ -238,6 +238,9 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
   __syncthreads();
   umma::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
+  // The schedule kernel runs just before this one (programmatic dependent
+  // launch): everything above overlapped it; its list and counter are read below.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int n_items = __ldg(p.sched_count) * p.n_heads;
   // Items reach the MMA and softmax warps through a small ring that the
   // producer fills from the ticket counter; -1 ends the list.
@@ -649,6 +652,9 @@ __global__ void __launch_bounds__(1024) prefill_schedule_kernel(const int32_t* _
                                                                 int n_bands, int capacity, int32_t* sched,
                                                                 int32_t* count, int* ticket, int* status) {
   __shared__ int band[kMaxBands];
+  // let the attention kernel start its prologue now; it waits for this grid
+  // to finish before it reads the schedule
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (threadIdx.x == 0) *ticket = 0;
   for (int m = threadIdx.x; m < n_bands; m += blockDim.x) band[m] = 0;
   __syncthreads();
@@ -728,7 +734,17 @@ int launch_tc(const PrefillParams& p, int total, int sched_capacity, CUtensorMap
   const long long items = (long long)p.n_mtiles * p.n_seqs * p.n_heads;
   const long long slots = (long long)(dev < 64 ? num_sms[dev] : 148) * C::kCtasPerSm;
   const int grid = (int)(items < slots ? items : slots);
-  kern<<<grid, 192, C::kSmemBytes, stream>>>(p, tq, tk, tv);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  TVK_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, p, tq, tk, tv));
   TVK_CHECK_LAUNCH("flash_prefill_tc");
   return TVK_OK;
 }
