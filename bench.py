@@ -520,12 +520,12 @@ def run_e2e8b(args, rank: int, world: int, local_rank: int) -> int:
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     else:
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         os.environ.setdefault("MASTER_PORT", "29533")
         dist.init_process_group("nccl", device_id=dev, rank=0, world_size=1,
-                                timeout=datetime.timedelta(seconds=300))
+                                timeout=datetime.timedelta(seconds=120))
     cfg = llama3_8b_config("bfloat16")
     model = Llama(cfg, device=dev, seed=1234 + 5)
     n_total, gen = 512, 256

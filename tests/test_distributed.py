@@ -113,7 +113,8 @@ def _worker(rank, world, port, mode, q):
         os.environ["MASTER_PORT"] = str(port)
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
         fail = 2 if (mode == "raise" and rank == 1) else None
-        eng = ShardedEngine(FakeEngine(fail_at_step=fail), rank, world, torch.device("cpu"))
+        mbs = 3 + 2 * rank if mode == "uneven" else 3
+        eng = ShardedEngine(FakeEngine(max_batch_size=mbs, fail_at_step=fail), rank, world, torch.device("cpu"))
         for p, m in zip(PROMPTS, MAX_TOKENS):
             eng.add_request(p, _Params(m))
         if mode == "die" and rank == 1:
@@ -171,6 +172,15 @@ def test_two_ranks_merge_to_the_single_rank_streams():
     owners = res[0][3]
     assert set(owners) == {0, 1} and owners == res[1][3]
     assert res[0][4] == res[1][4]                     # same number of collective steps
+
+
+@pytest.mark.slow
+def test_ranks_with_different_batch_sizes_agree_on_the_record_size():
+    """Each rank may size its engine to its own memory; the per-step all-gather
+    still needs one record size, so the ranks agree on the largest."""
+    res = _launch(2, "uneven")
+    assert all(r[1] == "ok" for r in res.values()), res
+    assert res[0][2] == res[1][2] == _single_rank_streams()
 
 
 @pytest.mark.slow

@@ -68,8 +68,15 @@ class ShardedEngine:
         self.next_request_id = 0
         self.load = [0] * world_size
         # tokens one rank can emit in one step: a prefill token per admitted sequence
-        # plus one per decode iteration per running sequence
-        self.capacity = engine.max_batch_size * (engine.num_scheduler_steps + 1)
+        # plus one per decode iteration per running sequence.  The all-gather needs
+        # one record size on every rank, and ranks may run engines of different
+        # batch sizes (each sizes its batch to its own memory), so take the largest.
+        cap = engine.max_batch_size * (engine.num_scheduler_steps + 1)
+        if world_size > 1 and dist.is_available() and dist.is_initialized():
+            t = torch.tensor([cap], dtype=torch.int64, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+            cap = int(t.item())
+        self.capacity = cap
         self.steps = 0
 
     # ------------------------------------------------------------------ API
