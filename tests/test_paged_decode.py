@@ -261,3 +261,47 @@ def test_without_workspace_matches_with(cuda, dtype):
     b = _call_abi(case, ws, ws.numel())
     assert torch.equal(a, b)
     _check(a, _oracle(case), dtype)
+
+
+def _subset_check(case, out, idx, dtype):
+    bt = case.block_tables[idx]
+    used = torch.unique(bt)
+    remap = torch.full((case.k_cache.shape[0],), -1, dtype=torch.int64, device=bt.device)
+    remap[used.long()] = torch.arange(len(used), device=bt.device)
+    sub_bt = remap[bt.long()].int()
+    ref = oa.paged_decode_attention(_np(case.q[idx]), _np(case.k_cache[used.long()]),
+                                    _np(case.v_cache[used.long()]), sub_bt.cpu().numpy(),
+                                    case.context_lens[idx].cpu().numpy(), case.n_heads, case.n_kv_heads,
+                                    case.head_dim, case.block_size)
+    _check(out[idx], ref, dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_persistent_plan_with_wide_tables_and_empty_sequences(cuda, dtype):
+    """A large batch (persistent CTAs, ticket counter) whose tables are far wider
+    than its contexts, with some empty sequences: the kernel sizes units from the
+    live contexts and empty sequences give zeros."""
+    from tinyvllm_b200 import _lib, workloads
+    rng = np.random.default_rng(31)
+    ctx = rng.integers(1, 300, size=256)
+    ctx[::17] = 0
+    case = workloads.decode_case(256, 32, 8, 128, 16, ctx.tolist(), dtype=dtype, device=cuda, seed=31, width=256)
+    plan = (__import__("ctypes").c_int * 4)()
+    assert _lib.lib().tvk_paged_decode_plan(256, 32, 8, 128, 16, 256, -1, _lib.dtype_code(case.q), plan) == 0
+    assert plan[3] == 1                               # persistent plan
+    out = _run(case)
+    zero = [i for i in range(256) if ctx[i] == 0]
+    assert torch.count_nonzero(out[zero]) == 0
+    _subset_check(case, out, [1, 2, 3, 50, 99, 128, 200, 254], dtype)   # 255 is empty
+
+
+def test_persistent_plan_with_a_sparse_long_tail(cuda):
+    """Most sequences short and a few long: the later splits are mostly dead
+    tickets, which the scan skips."""
+    ctx = [64] * 120 + [4000, 3000, 2500, 4096, 64, 1, 17, 4095]
+    from tinyvllm_b200 import workloads
+    case = workloads.decode_case(len(ctx), 32, 8, 128, 16, ctx, dtype=torch.float16, device=cuda, seed=32)
+    a = _run(case).clone()
+    b = _run(case)
+    assert torch.equal(a, b)
+    _subset_check(case, a, [0, 119, 120, 121, 122, 123, 124, 125, 126, 127], torch.float16)

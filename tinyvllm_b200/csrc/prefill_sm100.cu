@@ -114,16 +114,18 @@ struct PfCfg {
   // descriptor's block stride: after each stage's V tile at head_dim 128, one
   // shared block after all stages at head_dim 64 (stride = its distance).
   static constexpr int kVStageBytes = D == 128 ? kKvBytes + kKvBlockBytes : kKvBytes;
-  static constexpr int kStages = D == 64 ? 5 : 4;     // K/V ring depth (64-key tiles)
+  static constexpr int kStages = 4;                   // K/V ring depth (64-key tiles)
+  // two Q tiles: the next item's Q loads while this item's last scores compute
+  static constexpr int kQSlots = 2;
   static constexpr int kQOff = 0;
-  static constexpr int kKOff = kQOff + kQBytes;
+  static constexpr int kKOff = kQOff + kQSlots * kQBytes;
   static constexpr int kVOff = kKOff + kStages * kKvBytes;
   static constexpr int kOnesOff = kVOff + kStages * kVStageBytes;  // head_dim 64 only
   static constexpr int kBarOff = kOnesOff + (D == 64 ? kKvBlockBytes : 0);
-  // q_full, q_empty, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2], pv_done[2], o_empty, final,
+  // q_full[2], q_empty[2], k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2], pv_done[2], o_empty, final,
   // item_full[4], item_empty[4]
   static constexpr int kItemSlots = 4;
-  static constexpr int kNumBars = 2 + 3 * kStages + 6 + 2 + 2 * kItemSlots;
+  static constexpr int kNumBars = 2 * kQSlots + 3 * kStages + 6 + 2 + 2 * kItemSlots;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag, item ring
   static constexpr int kUsed = kMiscOff + 16 + 4 * kItemSlots;
   // head_dim 64: at most 113 KB so that two CTAs share an SM
@@ -181,8 +183,8 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
   }
   uint8_t* base = smem_raw + (base_u32 - raw_u32);
   uint64_t* q_full = reinterpret_cast<uint64_t*>(base + C::kBarOff);
-  uint64_t* q_empty = q_full + 1;
-  uint64_t* k_full = q_empty + 1;
+  uint64_t* q_empty = q_full + C::kQSlots;
+  uint64_t* k_full = q_empty + C::kQSlots;
   uint64_t* v_full = k_full + S;
   uint64_t* kv_empty = v_full + S;
   uint64_t* s_full = kv_empty + S;
@@ -202,8 +204,10 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
     umma::tmem_relinquish();
   }
   if (threadIdx.x == 0) {
-    ptx::mbar_init(q_full, 1);
-    ptx::mbar_init(q_empty, 1);
+    for (int i = 0; i < C::kQSlots; ++i) {
+      ptx::mbar_init(&q_full[i], 1);
+      ptx::mbar_init(&q_empty[i], 1);
+    }
     for (int s = 0; s < S; ++s) {
       ptx::mbar_init(&k_full[s], 1);
       ptx::mbar_init(&v_full[s], 1);
@@ -285,12 +289,14 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
       it = item_of(p, w);
       const int n_kv = kv_tiles(p, it);
       const int kvh = it.h / p.group;
-      ok = __all_sync(0xffffffffu, wait_or_abort(q_empty, (q_it & 1) ^ 1, abort_flag));
+      const int qs = q_it % C::kQSlots;
+      ok = __all_sync(0xffffffffu, wait_or_abort(&q_empty[qs], ((q_it / C::kQSlots) & 1) ^ 1, abort_flag));
       if (!ok) break;
       if (lane == 0) {
-        ptx::mbar_arrive_expect_tx(q_full, C::kQBytes);
+        ptx::mbar_arrive_expect_tx(&q_full[qs], C::kQBytes);
         for (int kb = 0; kb < C::kKB; ++kb)
-          tma_load_3d(base + C::kQOff + kb * C::kQBlockBytes, &tm_q, q_full, kb * 64, it.h, it.s0 + it.mtile * 128);
+          tma_load_3d(base + C::kQOff + qs * C::kQBytes + kb * C::kQBlockBytes, &tm_q, &q_full[qs], kb * 64, it.h,
+                      it.s0 + it.mtile * 128);
       }
       ++q_it;
       const bool write_kv = p.slot_mapping != nullptr && (it.h % p.group) == 0;
@@ -343,7 +349,8 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
         ptx::mbar_wait(&k_full[j % S], (j / S) & 1, 100000000ull);
         ptx::mbar_wait(&v_full[j % S], (j / S) & 1, 100000000ull);
       }
-      if (q_it > 0) ptx::mbar_wait(q_full, (q_it - 1) & 1, 100000000ull);
+      for (uint32_t j = q_it >= (uint32_t)C::kQSlots ? q_it - C::kQSlots : 0; j < q_it; ++j)
+        ptx::mbar_wait(&q_full[j % C::kQSlots], (j / C::kQSlots) & 1, 100000000ull);
     }
   } else if (warp == 1) {
     // =========================== MMA issuer =================================
@@ -353,7 +360,6 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
     if (lane == 0) {
       const uint32_t idesc_s = umma::idesc_f16(128, 64, kBf16, false);
       const uint32_t idesc_o = umma::idesc_f16(128, C::kOCols, kBf16, true);
-      const uint32_t q_addr = base_u32 + C::kQOff;
       uint32_t g = 0, q_it = 0, item_it = 0;
       bool ok = true;
       Item it;
@@ -383,7 +389,9 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
           break;
         }
         const int n_kv = kv_tiles(p, it);
-        ok = wait_or_abort(q_full, q_it & 1, abort_flag);
+        const int qs = q_it % C::kQSlots;
+        const uint32_t q_addr = base_u32 + C::kQOff + qs * C::kQBytes;
+        ok = wait_or_abort(&q_full[qs], (q_it / C::kQSlots) & 1, abort_flag);
         for (int j = 0; ok && j < n_kv; ++j, ++g) {
           const int st = g % S;
           const int sb = g & 1;
@@ -401,7 +409,7 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
             umma::mma_f16_ss(tmem + C::kSCol + sb * 64, ad, bd, idesc_s, ks > 0 ? 1u : 0u);
           }
           umma::commit(&s_full[sb]);
-          if (j == n_kv - 1) umma::commit(q_empty);  // Q is free once this item's S MMAs are done
+          if (j == n_kv - 1) umma::commit(&q_empty[qs]);  // Q is free once this item's S MMAs are done
           if (j >= 1) ok = issue_pv(g - 1, j == 1);
         }
         if (ok) ok = issue_pv(g - 1, n_kv == 1);
