@@ -95,7 +95,8 @@ struct TcCfg {
   static constexpr int kRingBytes = kStages * kStageBytes;
   static constexpr int kBarOffset = kRingBytes;             // full / empty barriers
   static constexpr int kMetaOffset = kRingBytes + 128;      // one int4 of unit data per stage
-  static constexpr int kQOffset = kRingBytes + 256;         // one query slot [group][D] per stage
+  static constexpr int kMergeBarOffset = kRingBytes + 256;  // two barriers of the per-unit merge
+  static constexpr int kQOffset = kRingBytes + 384;         // one query slot [group][D] per stage
   static_assert(2 * kStages * 8 <= 128 && kStages * 16 <= 128, "barrier / meta area");
   // merge scratch of the four consumer warps: m, l [4][16] then O [4][group][D]
   static __host__ __device__ constexpr int merge_offset(int group) { return kQOffset + kStages * group * D * 2; }
@@ -179,6 +180,7 @@ __global__ void __launch_bounds__(160, 2)
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(base + C::kBarOffset);
   uint64_t* empty_bar = full_bar + C::kStages;
   int4* meta = reinterpret_cast<int4*>(base + C::kMetaOffset);
+  uint64_t* merge_bar = reinterpret_cast<uint64_t*>(base + C::kMergeBarOffset);
   uint8_t* qslot = base + C::kQOffset;
   const int q_bytes = G * D * 2;
 
@@ -188,6 +190,8 @@ __global__ void __launch_bounds__(160, 2)
       ptx::mbar_init(&full_bar[s], 1);
       ptx::mbar_init(&empty_bar[s], 4);
     }
+    ptx::mbar_init(&merge_bar[0], 4);  // one arrival per consumer warp
+    ptx::mbar_init(&merge_bar[1], 4);
     ptx::fence_mbar_init();
   }
   __syncthreads();
@@ -357,6 +361,7 @@ __global__ void __launch_bounds__(160, 2)
   // ---------------- consumer warps ----------------------------------------
   const int g = lane >> 2, tig = lane & 3;
   float* cm = reinterpret_cast<float*>(base + C::merge_offset(G));
+  uint32_t n_merge = 0;
   float* cl = cm + 4 * 16;
   float* co = cl + 4 * 16;
 
@@ -497,7 +502,15 @@ __global__ void __launch_bounds__(160, 2)
     L0 += __shfl_xor_sync(0xffffffffu, L0, 2);
     float L1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
     L1 += __shfl_xor_sync(0xffffffffu, L1, 2);
-    ptx::named_barrier_sync(1, 128);  // the previous unit's merge has been read
+    // The four warps meet twice (bounded waits, so a warp that gave up cannot
+    // strand the others): first when all have read the previous unit's merge,
+    // then when all have written this one.
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(&merge_bar[0]);
+    if (!ptx::mbar_wait(&merge_bar[0], n_merge & 1)) {
+      report_timeout(p.status);
+      return;
+    }
     if (tig == 0) {
       cm[warp * 16 + g] = m0;
       cm[warp * 16 + g + 8] = m1;
@@ -516,7 +529,13 @@ __global__ void __launch_bounds__(160, 2)
         co[(warp * G + g + 8) * D + col + 1] = o[i][3];
       }
     }
-    ptx::named_barrier_sync(1, 128);
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(&merge_bar[1]);
+    if (!ptx::mbar_wait(&merge_bar[1], n_merge & 1)) {
+      report_timeout(p.status);
+      return;
+    }
+    ++n_merge;
 
     for (int idx = threadIdx.x; idx < G * D; idx += 128) {
       const int r = idx / D, col = idx % D;
