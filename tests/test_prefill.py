@@ -191,3 +191,26 @@ def test_repeat_calls_are_deterministic(cuda):
     b = flash_prefill_attention_varlen(q, k, v, cu, max(lens))
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("n", [33, 70])
+def test_many_prompts_take_the_device_schedule(cuda, n):
+    """More than 32 prompts: the work list is built by the schedule kernel rather
+    than by the producer warps; alternating with a small batch on the same
+    workspace checks that every call returns the item counters to zero."""
+    from tinyvllm_b200.attention import flash_prefill_attention_varlen
+    rng = np.random.default_rng(40 + n)
+    lens = [int(x) for x in rng.integers(1, 300, size=n)]
+    q, k, v, cu, _ = _config2_inputs(cuda, torch.float16, lens=lens)
+    small = _config2_inputs(cuda, torch.float16, lens=[130, 7, 260])
+    for _ in range(2):
+        out = flash_prefill_attention_varlen(q, k, v, cu, max(lens)).clone()
+        out_s = flash_prefill_attention_varlen(*small[:4], max(small[4])).clone()
+        torch.cuda.synchronize()
+        for i in (0, 1, n // 2, n - 1):
+            a, b = int(cu[i]), int(cu[i + 1])
+            _check(out[a:b], _oracle(q[a:b], k[a:b], v[a:b]), torch.float16)
+        sq, sk, sv, scu, slens = small
+        for i in range(3):
+            a, b = int(scu[i]), int(scu[i + 1])
+            _check(out_s[a:b], _oracle(sq[a:b], sk[a:b], sv[a:b]), torch.float16)
