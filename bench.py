@@ -432,7 +432,11 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
                    "timing": "CUDA-graph replay of the call (schedule + attention kernels) between events"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": None, "peak_kind": kind,
-                     "algorithmic_flops_per_launch": flops},
+                     "algorithmic_flops_per_launch": flops,
+                     # at head_dim 64 a 128x64 tile needs 8192 exponentials (512 cycles of
+                     # the 16/cycle MUFU unit) for 2.1 MFLOP of MMA work
+                     "exp_unit_bound_tflops": 2.0 * 2 * 128 * 64 * 64 / 512 * 148 * 1.965e9 / 1e12,
+                     "frac_of_exp_unit_bound": achieved / (2.0 * 2 * 128 * 64 * 64 / 512 * 148 * 1.965e9 / 1e12)},
         "cpu_baseline": cpu, "clocks": clk,
         "e2e": {"value": T / (e2e_ms / 1e3), "unit": "prompt tok/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
