@@ -214,3 +214,5 @@ def test_many_prompts_take_the_device_schedule(cuda, n):
         for i in range(3):
             a, b = int(scu[i]), int(scu[i + 1])
             _check(out_s[a:b], _oracle(sq[a:b], sk[a:b], sv[a:b]), torch.float16)
+    from tinyvllm_b200.attention import workspace_status
+    assert workspace_status(kind="prefill") == 0

@@ -45,6 +45,8 @@ struct PrefillParams {
   const int32_t* sched_count;   // tc path: number of entries in sched
   int* ticket;                  // tc path: next item to hand out (zeroed by the schedule kernel)
   int n_seqs, n_heads, n_kv_heads, group, head_dim, causal, num_blocks, block_size, n_mtiles;
+  int total_tokens;
+  int sched_cap;                // tc path: entries the schedule can hold
   float scale_log2;
 };
 
@@ -127,7 +129,7 @@ struct PfCfg {
   static constexpr int kItemSlots = 4;
   static constexpr int kNumBars = 2 * kQSlots + 3 * kStages + 6 + 2 + 2 * kItemSlots;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;  // tmem slot, abort flag, item ring
-  static constexpr int kUsed = kMiscOff + 16 + 4 * kItemSlots;
+  static constexpr int kUsed = kMiscOff + 16 + 32 * kItemSlots;  // 8 ints per ring slot
   // head_dim 64: at most 113 KB so that two CTAs share an SM
   // (2 x (113 + 1 reserved) KB = 228 KB); the slack above kUsed absorbs the
   // 1024-byte alignment of the base.
@@ -152,12 +154,19 @@ struct Item {
 
 // Item w of the schedule: query tiles sorted heaviest first, each expanded
 // over the query heads.  CTAs take items from the ticket counter as they free
-// up, so the heavy items start first and the light ones fill the gaps.
+// up, so the heavy items start first and the light ones fill the gaps.  The
+// schedule and the prompt offsets are read through L2 (the schedule kernel,
+// and possibly other work before it, wrote them while this grid was already
+// running its prologue); an entry that does not describe a query tile of a
+// prompt inside the token range comes back with seq = -1.
 __device__ __forceinline__ Item item_of(const PrefillParams& p, int w) {
-  const int e = __ldg(p.sched + w / p.n_heads);
+  const int e = __ldcg(p.sched + w / p.n_heads);
   const int seq = e >> 16, m = e & 0xFFFF;
-  const int s0 = __ldg(p.cu_seqlens + seq);
-  return Item{seq, m, w % p.n_heads, s0, __ldg(p.cu_seqlens + seq + 1) - s0};
+  if (seq < 0 || seq >= p.n_seqs || m >= p.n_mtiles) return Item{-1, 0, 0, 0, 0};
+  const int s0 = __ldcg(p.cu_seqlens + seq);
+  const int L = __ldcg(p.cu_seqlens + seq + 1) - s0;
+  if (s0 < 0 || L <= m * 128 || s0 + L > p.total_tokens) return Item{-1, 0, 0, 0, 0};
+  return Item{seq, m, w % p.n_heads, s0, L};
 }
 
 // 64-key tiles an item visits: up to and including the diagonal when causal.
@@ -196,7 +205,7 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
   uint64_t* item_empty = item_full + C::kItemSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + C::kMiscOff + 4);
-  volatile int* item_ring = reinterpret_cast<volatile int*>(base + C::kMiscOff + 16);
+  volatile int* item_ring = reinterpret_cast<volatile int*>(base + C::kMiscOff + 16);  // [slot][8]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 1) {
@@ -245,19 +254,18 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
   // The schedule kernel runs just before this one (programmatic dependent
   // launch): everything above overlapped it; its list and counter are read below.
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int n_items = __ldg(p.sched_count) * p.n_heads;
-  // Items reach the MMA and softmax warps through a small ring that the
-  // producer fills from the ticket counter; -1 ends the list.
+  const int n_items = min(__ldcg(p.sched_count), p.sched_cap) * p.n_heads;
+  // Items reach the MMA and softmax warps, decoded, through a small ring that
+  // the producer fills from the ticket counter; seq -1 ends the list.
   uint32_t n_seen = 0;
   auto take_item = [&](Item& it, bool arrive) -> int {  // 1: item, 0: end of list, -1: gave up
     const int slot = n_seen % C::kItemSlots;
     if (!wait_or_abort(&item_full[slot], (n_seen / C::kItemSlots) & 1, abort_flag)) return -1;
-    const int w = item_ring[slot];
+    volatile int* e = item_ring + slot * 8;
+    it = Item{e[0], e[1], e[2], e[3], e[4]};
     if (arrive) ptx::mbar_arrive(&item_empty[slot]);
     ++n_seen;
-    if (w < 0) return 0;
-    it = item_of(p, w);
-    return 1;
+    return it.seq < 0 ? 0 : 1;
   };
 
   if (warp == 0) {
@@ -271,22 +279,33 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
     }
     const long long n_slots = (long long)p.num_blocks * p.block_size;
     uint32_t n_claim = 0;
-    Item it;
+    Item it{};
     while (ok) {
       const int slot = n_claim % C::kItemSlots;
       int w = 0;
       if (lane == 0) w = (int)atomicAdd(p.ticket, 1);
       w = __shfl_sync(0xffffffffu, w, 0);
       if (w >= n_items) w = -1;
+      if (w >= 0) {
+        it = item_of(p, w);
+        if (it.seq < 0) {  // a corrupt schedule entry: stop here and say so
+          report(p.status);
+          w = -1;
+        }
+      }
       ok = __all_sync(0xffffffffu, wait_or_abort(&item_empty[slot], ((n_claim / C::kItemSlots) & 1) ^ 1, abort_flag));
       if (!ok) break;
       if (lane == 0) {
-        item_ring[slot] = w;
+        volatile int* e = item_ring + slot * 8;
+        e[0] = w < 0 ? -1 : it.seq;
+        e[1] = it.mtile;
+        e[2] = it.h;
+        e[3] = it.s0;
+        e[4] = it.L;
         ptx::mbar_arrive(&item_full[slot]);
       }
       ++n_claim;
       if (w < 0) break;
-      it = item_of(p, w);
       const int n_kv = kv_tiles(p, it);
       const int kvh = it.h / p.group;
       const int qs = q_it % C::kQSlots;
@@ -325,8 +344,8 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
           T* kc = reinterpret_cast<T*>(p.k_cache);
           T* vc = reinterpret_cast<T*>(p.v_cache);
           // one slot per lane for rows lane and lane + 32, shared by shuffles
-          const long long slot_lo = lane < rows ? p.slot_mapping[tok0 + lane] : -1;
-          const long long slot_hi = lane + 32 < rows ? p.slot_mapping[tok0 + lane + 32] : -1;
+          const long long slot_lo = lane < rows ? __ldcg(p.slot_mapping + tok0 + lane) : -1;
+          const long long slot_hi = lane + 32 < rows ? __ldcg(p.slot_mapping + tok0 + lane + 32) : -1;
           for (int i0 = 0; i0 < rows * (D / 8); i0 += 32) {
             const int i = i0 + lane;
             const int r = i / (D / 8), c8 = i % (D / 8);
@@ -821,6 +840,7 @@ extern "C" int tvk_flash_prefill_attention(const void* q, const void* k, const v
   p.num_blocks = num_blocks;
   p.block_size = block_size;
   p.n_mtiles = (max_seqlen + 127) / 128;
+  p.total_tokens = total_tokens;
   p.scale_log2 = (float)(1.4426950408889634 / sqrt((double)head_dim));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const bool tc = dtype != TVK_DTYPE_F32 && (head_dim == 64 || head_dim == 128);
@@ -840,6 +860,7 @@ extern "C" int tvk_flash_prefill_attention(const void* q, const void* k, const v
     p.ticket = w32 + 2;
     p.sched = w32 + tvk::kWorkspaceHeader / 4;
     const int cap = (int)((need - tvk::kWorkspaceHeader) / 4);
+    p.sched_cap = cap;
     if (dtype == TVK_DTYPE_F16)
       return head_dim == 64 ? launch_tc<__half, 64>(p, total_tokens, cap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, s)
                             : launch_tc<__half, 128>(p, total_tokens, cap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, s);
