@@ -84,9 +84,12 @@ def test_decode_plan(lib):
     assert lib.tvk_paged_decode_plan(256, 32, 8, 128, 16, 256, -1, 1, plan) == 0
     assert list(plan) == [4096, 1, 1, 1]
     # engine-sized call (64 sequences x 4 KV heads, 64-block tables): one CTA per
-    # 512-token unit, a combine for the second split
+    # (sequence, KV head), the whole 1024-token table as one unit, no combine
     assert lib.tvk_paged_decode_plan(64, 32, 4, 64, 16, 64, -1, 1, plan) == 0
-    assert list(plan) == [512, 2, 2, 0]
+    assert list(plan) == [1024, 1, 1, 0]
+    # fewer pairs: split to about one wave of CTAs, with a combine
+    assert lib.tvk_paged_decode_plan(16, 32, 4, 64, 16, 64, -1, 1, plan) == 0
+    assert plan[0] == 256 and plan[1] == 4 and plan[2] == 2 and plan[3] == 0
     # fp32 always takes the one-CTA-per-unit kernel
     assert lib.tvk_paged_decode_plan(256, 32, 8, 128, 16, 256, -1, 0, plan) == 0
     assert plan[3] == 0

@@ -112,11 +112,15 @@ constexpr int kDoneOffset = 128;
 constexpr int kSplitOffset = 192;
 
 // Resident tc CTAs on a B200 (two per SM), and the unit counts the split
-// policies aim for: about one and a half waves when every unit gets its own
-// CTA; about four units per resident CTA for persistent grids, enough for the
-// ticket counter to even out ragged contexts while keeping units long.
+// policies aim for: close to one wave when every unit gets its own CTA (a
+// small call gains more from skipping the split-K combine than from shorter
+// units: 64 sequences x 4 KV heads with contexts up to 640 take 11.8 us as one
+// 1024-token unit each, 15.6 us as 512-token units plus the combine); about
+// four units per resident CTA for persistent grids, enough for the ticket
+// counter to even out ragged contexts while keeping units long.
 constexpr long kSlots = 148L * 2;
-constexpr long kStaticTarget = 148L * 3;
+constexpr long kStaticTarget = 256;
+constexpr int kStaticMaxSplit = 1024;
 constexpr long kTargetUnits = kSlots * 4;
 constexpr int kMaxSplitTokens = 4096;
 
@@ -804,7 +808,7 @@ int split_for(long bk, int table_tok, int max_split, long target) {
 
 // How one call is cut into units and launched.
 //  * One CTA per unit (the simt kernel always; the tc kernel when that grid
-//    is at most two waves): units of up to 512 tokens, about 1.5 waves.
+//    is at most two waves): units of up to 1024 tokens, about one wave.
 //  * Otherwise persistent tc CTAs with the ticket counter: `split` is the
 //    smallest unit the kernel may use (it sizes the partials); the kernel
 //    picks the actual size from the live contexts.
@@ -815,7 +819,7 @@ struct Plan {
 Plan make_plan(int batch, int n_kv_heads, int table_tok, bool persistent_ok) {
   const long bk = (long)batch * n_kv_heads;
   Plan pl{};
-  pl.split = split_for(bk, table_tok, 512, kStaticTarget);
+  pl.split = split_for(bk, table_tok, kStaticMaxSplit, kStaticTarget);
   pl.max_splits = table_tok > 0 ? (table_tok + pl.split - 1) / pl.split : 1;
   pl.dynamic = 0;
   if (!persistent_ok || bk * pl.max_splits <= 2 * kSlots) return pl;
