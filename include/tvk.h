@@ -149,6 +149,20 @@ int tvk_rms_norm(const void* x, const void* residual, void* residual_out, const 
                  int rows, int dim, float eps, int dtype, void* stream);
 
 /*
+ * tvk_rms_norm plus the decode K/V append of one token per row, in one launch:
+ * row r's k and v rows ([rows, n_kv_heads, head_dim]) are stored at flat slot
+ * slots[r] of k_cache / v_cache [num_blocks, block_size, n_kv_heads, head_dim]
+ * (negative or out-of-pool slots skipped).  Replaces the post-attention write
+ * of Llama.decode (tinyvllm/model/llama.py:381-386) when the norm after the
+ * attention output projection is the next kernel, so the attention still reads
+ * the slot's previous contents as the reference does.
+ */
+int tvk_rms_norm_write_kv(const void* x, const void* residual, void* residual_out, const void* weight, void* out,
+                          int rows, int dim, float eps, const void* k, const void* v, const int64_t* slots,
+                          void* k_cache, void* v_cache, int n_kv_heads, int head_dim, int num_blocks,
+                          int block_size, int dtype, void* stream);
+
+/*
  * In-place interleaved-pair RoPE on q [n_tokens, n_heads, head_dim] and
  * k [n_tokens, n_kv_heads, head_dim], apply_rope (llama.py:34-55):
  *   (x[2i], x[2i+1]) -> (x0 c - x1 s, x0 s + x1 c),  c/s = table[positions[t], i]

@@ -146,6 +146,37 @@ def test_write_kv_slots_and_fused_rope(cuda, dtype):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("hkv,d", [(4, 64), (8, 128)])
+def test_rms_norm_write_kv_matches_separate_ops(cuda, dtype, hkv, d):
+    """rms_norm(write_kv=...) == rms_norm(residual=...) then tvk_write_kv_slots, bit for bit."""
+    from tinyvllm_b200.layers import rms_norm, write_kv_slots
+    g = _gen(cuda, 33 + d)
+    B, dim = 10, 2048
+    x = torch.randn(B, dim, generator=g, device=cuda).to(dtype)
+    r = torch.randn(B, dim, generator=g, device=cuda).to(dtype)
+    w = (1 + 0.1 * torch.randn(dim, generator=g, device=cuda)).to(dtype)
+    k = torch.randn(B, hkv, d, generator=g, device=cuda).to(dtype)
+    v = torch.randn(B, hkv, d, generator=g, device=cuda).to(dtype)
+    slots = torch.tensor([5, 17, 0, -1, 63, 40, 41, 42, 1000, 7], dtype=torch.int64, device=cuda)
+    kc1 = torch.randn(4, 16, hkv, d, generator=g, device=cuda).to(dtype)
+    vc1 = torch.randn(4, 16, hkv, d, generator=g, device=cuda).to(dtype)
+    kc2, vc2 = kc1.clone(), vc1.clone()
+    r1, r2 = r.clone(), r.clone()
+    out1 = rms_norm(x, w, 1e-5, residual=r1)
+    write_kv_slots(k, v, slots, kc1, vc1)
+    out2 = rms_norm(x, w, 1e-5, residual=r2, write_kv=(k, v, slots, kc2, vc2))
+    torch.cuda.synchronize()
+    assert torch.equal(out1, out2) and torch.equal(r1, r2)
+    assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
+    flat_k, flat_v = kc2.view(-1, hkv, d), vc2.view(-1, hkv, d)
+    for t, s in enumerate(slots.tolist()):
+        if 0 <= s < 64:
+            assert torch.equal(flat_k[s], k[t]) and torch.equal(flat_v[s], v[t])
+    with pytest.raises(ValueError):
+        rms_norm(x, w, residual=r2, write_kv=(k, v, slots[:3], kc2, vc2))
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("with_slots", [False, True])
 def test_qkv_rope_matches_separate_ops(cuda, dtype, with_slots):
     """One packed projection row split + RoPE == slicing then tvk_rope (and tvk_write_kv_slots)."""

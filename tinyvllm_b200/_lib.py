@@ -33,6 +33,8 @@ SIGNATURES = {
     "tvk_selftest_umma_gemm": (_c_int, [_c_void] * 3 + [_c_int] * 5 + [_c_void, _c_void]),
     "tvk_paged_decode_attention_noalloc": (_c_int, [_c_void] * 6 + [_c_int] * 9 + [_c_void]),
     "tvk_rms_norm": (_c_int, [_c_void] * 5 + [_c_int, _c_int, _c_float, _c_int, _c_void]),
+    "tvk_rms_norm_write_kv": (_c_int, [_c_void] * 5 + [_c_int, _c_int, _c_float] + [_c_void] * 5 +
+                              [_c_int] * 5 + [_c_void]),
     "tvk_rope": (_c_int, [_c_void] * 5 + [_c_int] * 6 + [_c_void]),
     "tvk_rope_write_kv": (_c_int, [_c_void] * 9 + [_c_int] * 8 + [_c_void]),
     "tvk_write_kv_slots": (_c_int, [_c_void] * 5 + [_c_int] * 6 + [_c_void]),

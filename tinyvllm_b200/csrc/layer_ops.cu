@@ -60,13 +60,38 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 constexpr int kNormThreads = 256;
 constexpr int kNormMaxVec = 8;  // per thread: dim <= 256 * 8 * N
 
+// Optional K/V append carried by the norm kernel (slots null: none).
+template <typename T>
+struct KvAppend {
+  const T* k;
+  const T* v;
+  const int64_t* slots;
+  T* k_cache;
+  T* v_cache;
+  int row_elems;       // n_kv_heads * head_dim
+  long long n_slots;   // num_blocks * block_size
+};
+
 template <typename T>
 __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const T* __restrict__ x, const T* residual,
                                                                 T* residual_out, const T* __restrict__ w,
-                                                                T* __restrict__ out, int dim, float eps) {
+                                                                T* __restrict__ out, int dim, float eps,
+                                                                KvAppend<T> kv) {
   constexpr int N = Vec<T>::N;
   __shared__ float red[32];
   const size_t row = blockIdx.x;
+  if (kv.slots) {
+    // This row's new k and v rows go to its paged slot (decode append done
+    // after the attention that read the slot's old contents).
+    const long long slot = kv.slots[row];
+    if (slot >= 0 && slot < kv.n_slots) {
+      for (int i = threadIdx.x; i < kv.row_elems / N; i += kNormThreads) {
+        const size_t src = row * kv.row_elems + (size_t)i * N, dst = (size_t)slot * kv.row_elems + (size_t)i * N;
+        *reinterpret_cast<uint4*>(kv.k_cache + dst) = *reinterpret_cast<const uint4*>(kv.k + src);
+        *reinterpret_cast<uint4*>(kv.v_cache + dst) = *reinterpret_cast<const uint4*>(kv.v + src);
+      }
+    }
+  }
   const T* xr = x + row * dim;
   const int nvec = dim / N;
   float v[kNormMaxVec][N];
@@ -392,8 +417,35 @@ extern "C" int tvk_rms_norm(const void* x, const void* residual, void* residual_
                 aligned16(residual_out))), "pointers must be 16-byte aligned");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   TVK_DISPATCH(dtype, rms_norm_kernel<T><<<rows, kNormThreads, 0, s>>>(
-      (const T*)x, (const T*)residual, (T*)residual_out, (const T*)weight, (T*)out, dim, eps));
+      (const T*)x, (const T*)residual, (T*)residual_out, (const T*)weight, (T*)out, dim, eps, KvAppend<T>{}));
   TVK_CHECK_LAUNCH("rms_norm");
+  return TVK_OK;
+}
+
+extern "C" int tvk_rms_norm_write_kv(const void* x, const void* residual, void* residual_out, const void* weight,
+                                     void* out, int rows, int dim, float eps, const void* k, const void* v,
+                                     const int64_t* slots, void* k_cache, void* v_cache, int n_kv_heads,
+                                     int head_dim, int num_blocks, int block_size, int dtype, void* stream) {
+  TVK_CHECK_ARG(rows >= 0 && dim > 0, "bad shape rows=%d dim=%d", rows, dim);
+  if (rows == 0) return TVK_OK;
+  TVK_CHECK_ARG(x && weight && out && k && v && slots && k_cache && v_cache, "null pointer argument");
+  TVK_CHECK_ARG(!residual == !residual_out, "residual and residual_out go together");
+  const int N = vec_elems(dtype);
+  TVK_CHECK_ARG(dim % N == 0 && dim / N <= kNormThreads * kNormMaxVec,
+                "dim %d must be a multiple of %d and at most %d", dim, N, N * kNormThreads * kNormMaxVec);
+  TVK_CHECK_ARG(n_kv_heads > 0 && head_dim > 0 && (n_kv_heads * head_dim) % N == 0,
+                "n_kv_heads * head_dim must be a positive multiple of %d", N);
+  TVK_CHECK_ARG(num_blocks > 0 && block_size > 0, "num_blocks and block_size must be positive");
+  TVK_CHECK_ARG(aligned16(x) && aligned16(weight) && aligned16(out) && aligned16(k) && aligned16(v) &&
+                    aligned16(k_cache) && aligned16(v_cache) &&
+                    (!residual || (aligned16(residual) && aligned16(residual_out))),
+                "pointers must be 16-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  TVK_DISPATCH(dtype, rms_norm_kernel<T><<<rows, kNormThreads, 0, s>>>(
+      (const T*)x, (const T*)residual, (T*)residual_out, (const T*)weight, (T*)out, dim, eps,
+      KvAppend<T>{(const T*)k, (const T*)v, slots, (T*)k_cache, (T*)v_cache, n_kv_heads * head_dim,
+                  (long long)num_blocks * block_size}));
+  TVK_CHECK_LAUNCH("rms_norm_write_kv");
   return TVK_OK;
 }
 

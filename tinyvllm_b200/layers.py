@@ -36,18 +36,34 @@ def precompute_freqs_cis(dim: int, seq_len: int, theta: float = 10000.0,
 
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-5, *,
-             residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+             residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+             write_kv: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]] = None
+             ) -> torch.Tensor:
     """RMSNorm (llama.py:21-23) over the last dim.  With ``residual`` the kernel first
-    forms ``residual += x`` (in place, rounded to the dtype) and normalises that sum."""
-    dev = _lib.require_cuda(x, weight, *(t for t in (residual, out) if t is not None))
-    _contig(x, weight, residual, out)
+    forms ``residual += x`` (in place, rounded to the dtype) and normalises that sum.
+    With ``write_kv = (k, v, slots, k_cache, v_cache)`` the same launch also stores
+    row r's k/v rows [rows, Hkv, D] at pool slot slots[r] (the decode K/V append of
+    llama.py:381-386, after the attention that read the slot's old contents)."""
+    extra = write_kv if write_kv is not None else ()
+    dev = _lib.require_cuda(x, weight, *(t for t in (residual, out) if t is not None), *extra)
+    _contig(x, weight, residual, out, *extra)
     dim = x.shape[-1]
     rows = x.numel() // dim
     if out is None:
         out = torch.empty_like(x)
-    rc = _lib.lib().tvk_rms_norm(_lib.ptr(x), _lib.ptr(residual), _lib.ptr(residual), _lib.ptr(weight),
-                                 _lib.ptr(out), rows, dim, float(eps), _lib.dtype_code(x), _stream(dev))
-    _lib.check(rc, "tvk_rms_norm")
+    if write_kv is None:
+        rc = _lib.lib().tvk_rms_norm(_lib.ptr(x), _lib.ptr(residual), _lib.ptr(residual), _lib.ptr(weight),
+                                     _lib.ptr(out), rows, dim, float(eps), _lib.dtype_code(x), _stream(dev))
+        _lib.check(rc, "tvk_rms_norm")
+        return out
+    k, v, slots, kc, vc = write_kv
+    if slots.dtype != torch.int64 or slots.numel() != rows or k.shape[0] != rows:
+        raise ValueError("write_kv needs one int64 slot and one k/v row per norm row")
+    rc = _lib.lib().tvk_rms_norm_write_kv(
+        _lib.ptr(x), _lib.ptr(residual), _lib.ptr(residual), _lib.ptr(weight), _lib.ptr(out), rows, dim, float(eps),
+        _lib.ptr(k), _lib.ptr(v), _lib.ptr(slots), _lib.ptr(kc), _lib.ptr(vc), kc.shape[2], kc.shape[3], kc.shape[0],
+        kc.shape[1], _lib.dtype_code(x), _stream(dev))
+    _lib.check(rc, "tvk_rms_norm_write_kv")
     return out
 
 

@@ -167,10 +167,12 @@ class Llama:
 
     # ------------------------------------------------------------------ blocks
     def _layer_ffn(self, L: LayerWeights, h: torch.Tensor, attn: torch.Tensor, next_norm: torch.Tensor,
-                   T: int) -> torch.Tensor:
+                   T: int, write_kv=None) -> torch.Tensor:
+        """O-projection, residual + ffn_norm, SwiGLU FFN, residual + next norm.  ``write_kv``
+        (k, v, slots, k_cache, v_cache) rides on the first norm's launch."""
         c = self.config
         o = torch.matmul(attn.view(T, c.n_heads * c.head_dim), L.wo)
-        x = layers.rms_norm(o, L.ffn_norm, c.norm_eps, residual=h)       # h += o; x = ffn_norm(h)
+        x = layers.rms_norm(o, L.ffn_norm, c.norm_eps, residual=h, write_kv=write_kv)  # h += o; x = ffn_norm(h)
         gu = torch.matmul(x, L.w13)
         a = layers.silu_mul(gu[:, :c.hidden_dim], gu[:, c.hidden_dim:])
         f = torch.matmul(a, L.w2)
@@ -236,10 +238,11 @@ class Llama:
                 q, k, v = self._qkv(L, x, positions)
             attn = paged_decode_attention(q.view(B, 1, c.n_heads, c.head_dim), kc, vc, block_tables, context_lens,
                                           c.n_heads, c.n_kv_heads, c.head_dim, kv_cache.block_size)
-            if kv_order != "append_first":
-                layers.write_kv_slots(k, v, slots, kc, vc)
+            # reference order: the new token's K/V reaches the pool after the attention
+            # (llama.py:381-386), stored by the launch of the norm that follows wo
+            late_kv = (k, v, slots, kc, vc) if kv_order != "append_first" else None
             nxt = self.layers[i + 1].attention_norm if i + 1 < c.n_layers else self.norm
-            x = self._layer_ffn(L, h, attn, nxt, B)
+            x = self._layer_ffn(L, h, attn, nxt, B, write_kv=late_kv)
         return torch.matmul(x, self.output)
 
 
