@@ -366,20 +366,24 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    lens = PREFILL_LENS
+    lens = tuple(int(x) for x in args.prefill_lens.split(",")) if args.prefill_lens else PREFILL_LENS
+    hq, hkv, hd = 32, args.prefill_kv_heads, args.prefill_head_dim
+    dt = torch.bfloat16 if args.prefill_dtype == "bf16" else torch.float16
+    is_cfg2 = lens == PREFILL_LENS and (hkv, hd, dt) == (4, 64, torch.float16)
     T = sum(lens)
     g = torch.Generator(device=dev).manual_seed(1236 + rank)
-    q = torch.randn(T, 32, 64, generator=g, device=dev).half()
-    k = torch.randn(T, 4, 64, generator=g, device=dev).half()
-    v = torch.randn(T, 4, 64, generator=g, device=dev).half()
+    q = torch.randn(T, hq, hd, generator=g, device=dev).to(dt)
+    k = torch.randn(T, hkv, hd, generator=g, device=dev).to(dt)
+    v = torch.randn(T, hkv, hd, generator=g, device=dev).to(dt)
     cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=dev)
-    bm = BlockManager(1, 1024, 16)
+    n_blocks = max(1024, sum((L + 15) // 16 for L in lens))
+    bm = BlockManager(1, n_blocks, 16)
     slots = []
     for sid, L in enumerate(lens):
         bm.register_sequence(sid)
         slots.append(bm.slot_mapping(sid, 0, L))
     slots = torch.from_numpy(np.concatenate(slots)).to(dev)
-    kc = torch.zeros(1024, 16, 4, 64, dtype=torch.float16, device=dev)
+    kc = torch.zeros(n_blocks, 16, hkv, hd, dtype=dt, device=dev)
     vc = torch.zeros_like(kc)
     out = torch.empty_like(q)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)   # > 126 MB L2
@@ -454,11 +458,11 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
     if rank != 0:
         return 0
     ms = statistics.mean(per_step)
-    flops = 4.0 * 32 * 64 * sum(L * (L + 1) / 2 for L in lens)
+    flops = 4.0 * hq * hd * sum(L * (L + 1) / 2 for L in lens)
     achieved = flops / (ms / 1e3) / 1e12
     peak, kind = _tensor_peak()
     cpu = None
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and is_cfg2:
         from oracle import attention as oa
         qn, kn, vn = q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy()
         t0 = time.perf_counter()
@@ -469,21 +473,24 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
         cpu = {"value": T / dt, "unit": "prompt tok/s", "cores": os.cpu_count() or 1, "kind": "port",
                "sample": "all 8 config-2 prompts once, numpy restatement of llama.py:58-94"}
     line = {
-        "metric": "flash-prefill attention: prompt tok/s (config 2, one ragged call per step)",
+        "metric": "flash-prefill attention: prompt tok/s (" + ("config 2" if is_cfg2 else "custom prompts") +
+                  ", one ragged call per step)",
         "value": T / (ms / 1e3), "unit": "prompt tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16" if dt == torch.bfloat16 else "f16",
         "data": "synthetic",
-        "config": {"workload": "config2 causal prefill, 8 prompts L=" + ",".join(map(str, lens)) +
-                               ", 32q/4kv heads, D=64, fp16, paged write into 1024 blocks",
+        "config": {"workload": ("config2" if is_cfg2 else "custom") + f" causal prefill, {len(lens)} prompts L=" +
+                               ",".join(map(str, lens)) + f", {hq}q/{hkv}kv heads, D={hd}, " +
+                               ("bf16" if dt == torch.bfloat16 else "fp16") + f", paged write into {n_blocks} blocks",
                    "l2": "flushed between steps (256 MB write, then read back; outside the events)",
                    "timing": "CUDA-graph replay of the call (schedule + attention kernels) between events"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "traffic": None, "peak_kind": kind,
                      "algorithmic_flops_per_launch": flops,
-                     # at head_dim 64 a 128x64 tile needs 8192 exponentials (512 cycles of
-                     # the 16/cycle MUFU unit) for 2.1 MFLOP of MMA work
-                     "exp_unit_bound_tflops": 2.0 * 2 * 128 * 64 * 64 / 512 * 148 * 1.965e9 / 1e12,
-                     "frac_of_exp_unit_bound": achieved / (2.0 * 2 * 128 * 64 * 64 / 512 * 148 * 1.965e9 / 1e12)},
+                     # a 128x64 tile needs 8192 exponentials (512 cycles of the 16/cycle
+                     # MUFU unit) for 2 * 2 * 128 * 64 * head_dim FLOP of MMA work
+                     "exp_unit_bound_tflops": 2.0 * 2 * 128 * 64 * hd / 512 * 148 * 1.965e9 / 1e12,
+                     "frac_of_exp_unit_bound": achieved / (2.0 * 2 * 128 * 64 * hd / 512 * 148 * 1.965e9 / 1e12)},
         "cpu_baseline": cpu, "clocks": clk,
         "e2e": {"value": T / (e2e_ms / 1e3), "unit": "prompt tok/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
@@ -706,6 +713,11 @@ def main() -> int:
     ap.add_argument("--workload", choices=["decode", "prefill", "e2e", "e2e8b"], default="decode",
                     help="decode = config 3 paged decode (the headline); prefill = config 2 flash prefill; "
                          "e2e = config 4 TinyLlama engine; e2e8b = config 5 sharded Llama-3-8B-shape decode")
+    ap.add_argument("--prefill-lens", default=None,
+                    help="prefill workload: comma-separated prompt lengths (default: config 2's eight prompts)")
+    ap.add_argument("--prefill-head-dim", type=int, choices=[64, 128], default=64)
+    ap.add_argument("--prefill-kv-heads", type=int, default=4, help="prefill workload: KV heads (32 query heads)")
+    ap.add_argument("--prefill-dtype", choices=["fp16", "bf16"], default="fp16")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
