@@ -108,6 +108,49 @@ class ClockSampler:
                 "power_w_max": max((num(r[3]) or 0.0) for r in rows)}
 
 
+_BLAS_LIMITS = None
+
+
+def _all_host_threads() -> int:
+    """Let the BLAS behind numpy use every host core and return the threads it now
+    uses.  torchrun exports OMP_NUM_THREADS=1 to each rank, which would otherwise
+    leave the CPU restatement single-threaded under --gpus N > 1."""
+    global _BLAS_LIMITS
+    try:
+        from threadpoolctl import threadpool_info, threadpool_limits
+        _BLAS_LIMITS = threadpool_limits(limits=os.cpu_count() or 1, user_api="blas")
+        n = max((int(i.get("num_threads", 1)) for i in threadpool_info() if i.get("user_api") == "blas"), default=1)
+        return max(n, 1)
+    except Exception:   # no threadpoolctl: report what the environment allows
+        return int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+
+
+def _fastest_blas_threads(call) -> int:
+    """Time one call with every host core and one with a single BLAS thread (the
+    restatement's matmuls are small, and on some hosts threading only costs), keep
+    the faster setting for the timed calls and return its thread count."""
+    global _BLAS_LIMITS
+    n_all = _all_host_threads()
+    t0 = time.perf_counter()
+    call()
+    t_all = time.perf_counter() - t0
+    if n_all <= 1:
+        return 1
+    try:
+        from threadpoolctl import threadpool_limits
+    except Exception:
+        return n_all
+    one = threadpool_limits(limits=1, user_api="blas")
+    t0 = time.perf_counter()
+    call()
+    t_one = time.perf_counter() - t0
+    if t_one < t_all:
+        _BLAS_LIMITS = one
+        return 1
+    one.restore_original_limits()
+    return _all_host_threads()
+
+
 def cpu_baseline_sample(n_seqs: int = CPU_SAMPLE_SEQS, reps: int = 5):
     """Time the oracle restatement of the reference path on a bounded sample of
     config 3: the first ``n_seqs`` sequences with their own blocks, on the host."""
@@ -120,16 +163,17 @@ def cpu_baseline_sample(n_seqs: int = CPU_SAMPLE_SEQS, reps: int = 5):
     vc = case.v_cache.float().numpy()
     bt = case.block_tables.numpy()
     ctx = case.context_lens.numpy()
-    oa.paged_decode_attention(q, kc, vc, bt, ctx, 32, 8, 128, 16)   # warm-up
+    threads = _fastest_blas_threads(lambda: oa.paged_decode_attention(q, kc, vc, bt, ctx, 32, 8, 128, 16))
     times = []
     for _ in range(reps):
         t0 = time.perf_counter()
         oa.paged_decode_attention(q, kc, vc, bt, ctx, 32, 8, 128, 16)
         times.append(time.perf_counter() - t0)
     med = statistics.median(times)
-    cores = os.cpu_count() or 1
+    cores = threads
     sample = (f"first {n_seqs} sequences of config 3 (ctx sum {int(ctx.sum())}, table width "
-              f"{bt.shape[1]} blocks), numpy restatement of llama.py:97-144, median of {reps}")
+              f"{bt.shape[1]} blocks), numpy restatement of llama.py:97-144, median of {reps}, "
+              f"{threads} BLAS thread(s), the faster of one and all host cores")
     return {"value": n_seqs / med, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
             "seconds_per_call": med}
 
@@ -147,6 +191,7 @@ def run_reference(args, rank: int, world: int) -> int:
     vc = case.v_cache.float().numpy()
     bt = case.block_tables.numpy()
     ctx = case.context_lens.numpy()
+    threads = _fastest_blas_threads(lambda: oa.paged_decode_attention(q, kc, vc, bt, ctx, 32, 8, 128, 16))
     for _ in range(args.warmup):
         oa.paged_decode_attention(q, kc, vc, bt, ctx, 32, 8, 128, 16)
     t0 = time.perf_counter()
@@ -154,7 +199,7 @@ def run_reference(args, rank: int, world: int) -> int:
         oa.paged_decode_attention(q, kc, vc, bt, ctx, 32, 8, 128, 16)
     dt = (time.perf_counter() - t0) / args.steps
     value = n / dt
-    cores = os.cpu_count() or 1
+    cores = threads
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
@@ -163,7 +208,8 @@ def run_reference(args, rank: int, world: int) -> int:
                    "n_kv_heads": 8, "head_dim": 128, "block_size": 16, "ctx": "U{128..4096}"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": f"first {n} sequences of config 3 per step; tinygrad absent, so the numpy "
-                                   "restatement of llama.py:97-144 with all host BLAS threads"},
+                                   f"restatement of llama.py:97-144 on {threads} BLAS thread(s), the faster "
+                                   "of one and all host cores"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -464,13 +510,14 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
     cpu = None
     if not args.no_cpu_baseline and is_cfg2:
         from oracle import attention as oa
+        threads = _all_host_threads()
         qn, kn, vn = q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy()
         t0 = time.perf_counter()
         for i, L in enumerate(lens):
             a, b = int(cu[i]), int(cu[i + 1])
             oa.flash_prefill_attention(qn[None, a:b], kn[None, a:b], vn[None, a:b], True)
         dt = time.perf_counter() - t0
-        cpu = {"value": T / dt, "unit": "prompt tok/s", "cores": os.cpu_count() or 1, "kind": "port",
+        cpu = {"value": T / dt, "unit": "prompt tok/s", "cores": threads, "kind": "port",
                "sample": "all 8 config-2 prompts once, numpy restatement of llama.py:58-94"}
     line = {
         "metric": "flash-prefill attention: prompt tok/s (" + ("config 2" if is_cfg2 else "custom prompts") +
@@ -511,6 +558,7 @@ def e2e_cpu_baseline(model, n_req: int = 8, prompt_len: int = 32, gen: int = 16)
     om = OracleLlama(model.numpy_weights(), c.n_layers, c.n_heads, c.n_kv_heads, c.head_dim, c.norm_eps,
                      c.rope_theta, prompt_len + gen + 16)
     eng = OracleEngine(om, max_batch_size=n_req, num_blocks=n_req * 8, block_size=16)
+    threads = _all_host_threads()
     rng = np.random.default_rng(4321)
     for _ in range(n_req):
         eng.add_request(rng.integers(3, c.vocab_size, size=prompt_len).tolist(), gen)
@@ -518,7 +566,7 @@ def e2e_cpu_baseline(model, n_req: int = 8, prompt_len: int = 32, gen: int = 16)
     while eng.has_unfinished():
         eng.step()
     dt = time.perf_counter() - t0
-    return {"value": n_req * gen / dt, "unit": "tok/s", "cores": os.cpu_count() or 1, "kind": "port",
+    return {"value": n_req * gen / dt, "unit": "tok/s", "cores": threads, "kind": "port",
             "sample": f"{n_req} requests x {prompt_len}-token prompts x {gen} greedy tokens (prefill included), "
                       "numpy restatement of the reference engine and model with the same weights"}
 
