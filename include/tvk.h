@@ -259,6 +259,30 @@ int tvk_paged_decode_attention_noalloc(const void* q, const void* k_cache, const
                                        int max_context_len, int dtype, void* stream);
 
 /*
+ * Status word of the no-allocation entry point on the current device: waits
+ * for `stream`, then stores the word at *status (host memory).  0 = the last
+ * tvk_paged_decode_attention_noalloc call on this device completed; non-zero =
+ * a bounded wait inside its kernel gave up (after 2 s) and its output is
+ * incomplete.  The next no-allocation call on the device clears the word.
+ * Allocates nothing.  No counterpart in the reference (tinygrad raises on the host).
+ */
+int tvk_paged_decode_noalloc_status(int* status, void* stream);
+
+/*
+ * Test hook for the kernels' bounded waits (no counterpart in the reference).
+ * Arms the next tvk_paged_decode_attention / tvk_flash_prefill_attention call
+ * made on the calling thread that reaches a tensor-core kernel (fp16/bf16):
+ * that launch gets `limit_ns` (1e5 .. 2e9) as the wall-time limit of its
+ * mbarrier waits, and its producer warp issues no loads, so the consumers'
+ * first wait runs out.  The kernel then sets the workspace status word to 1
+ * and returns; nothing faults, traps or hangs.  The caller must zero the
+ * workspace header (256 bytes) before the next call.  One-shot: the arming is
+ * consumed by the next decode or prefill call on the thread that passes its
+ * argument checks (an fp32 call consumes it without effect).
+ */
+int tvk_debug_arm_wait_timeout(long long limit_ns);
+
+/*
  * Tensor-core layout self-test (no reference counterpart): one 128 x n x k
  * tcgen05 GEMM through the operand paths the prefill kernel uses (A written
  * swizzled into shared memory by threads, or into TMEM with tcgen05.st when

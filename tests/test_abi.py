@@ -128,3 +128,13 @@ def test_cpu_tensors_are_refused():
     with pytest.raises(RuntimeError, match="CUDA"):
         paged_decode_attention(q, kc, kc, torch.zeros(1, 2, dtype=torch.int32),
                                torch.ones(1, dtype=torch.int32), 4, 4, 32, 16)
+
+
+def test_wait_test_hook_rejects_limits_out_of_range(lib):
+    assert lib.tvk_debug_arm_wait_timeout(10) == -1
+    assert lib.tvk_debug_arm_wait_timeout(3_000_000_000) == -1
+    assert b"wait limit" in lib.tvk_last_error()
+
+
+def test_noalloc_status_rejects_null(lib):
+    assert lib.tvk_paged_decode_noalloc_status(None, None) == -1

@@ -50,30 +50,33 @@ def test_noalloc_matches_workspace_entry_two_calls(cuda):
     b = workloads.decode_case(5, 32, 4, 64, 16, [3, 70, 300, 900, 1500], dtype=torch.float32, device=cuda, seed=21)
     out_a = torch.full_like(a.q, float("nan"))
     out_b = torch.full_like(b.q, float("nan"))
+    status = ctypes.c_int(-1)
+    stream = torch.cuda.current_stream().cuda_stream
     assert _noalloc(lib, a, out_a) == 0, lib.tvk_last_error()
+    assert lib.tvk_paged_decode_noalloc_status(ctypes.byref(status), stream) == 0 and status.value == 0
     assert _noalloc(lib, b, out_b) == 0, lib.tvk_last_error()
+    assert lib.tvk_paged_decode_noalloc_status(ctypes.byref(status), stream) == 0 and status.value == 0
     torch.cuda.synchronize()
     _close(out_a, _with_workspace(a), a.q.dtype)
     _close(out_b, _with_workspace(b), b.q.dtype)
     # and once more on the first case, after the scratch held the second call's partials
     out_a2 = torch.full_like(a.q, float("nan"))
     assert _noalloc(lib, a, out_a2) == 0, lib.tvk_last_error()
+    assert lib.tvk_paged_decode_noalloc_status(ctypes.byref(status), stream) == 0 and status.value == 0
     torch.cuda.synchronize()
     _close(out_a2, out_a, a.q.dtype)
 
 
 def test_noalloc_refuses_calls_beyond_its_scratch(cuda):
-    from tinyvllm_b200 import _lib, workloads
+    from tinyvllm_b200 import _lib
     lib = _lib.lib()
-    case = workloads.decode_case(2, 32, 8, 128, 16, [10, 20], dtype=torch.float16, device=cuda, seed=22)
     need = lib.tvk_paged_decode_workspace_size(4096, 32, 8, 128, 16, 4096, -1)
     assert need > (64 << 20)
-    out = torch.zeros_like(case.q)
     stream = torch.cuda.current_stream().cuda_stream
-    # claim a batch of 4096 with 4096-block tables: refused before any launch
-    rc = lib.tvk_paged_decode_attention_noalloc(
-        case.q.data_ptr(), case.k_cache.data_ptr(), case.v_cache.data_ptr(), case.block_tables.data_ptr(),
-        case.context_lens.data_ptr(), out.data_ptr(), 4096, 32, 8, 128, 16, case.k_cache.shape[0], 4096, -1, 1,
-        stream)
+    # a batch of 4096 with 4096-block tables is refused by the size guard before any
+    # launch; the buffers are null, so a regressed guard would still be stopped by the
+    # null-pointer check instead of launching over undersized buffers
+    rc = lib.tvk_paged_decode_attention_noalloc(None, None, None, None, None, None, 4096, 32, 8, 128, 16, 1000,
+                                                4096, -1, 1, stream)
     assert rc == -4
     assert b"fixed" in lib.tvk_last_error()

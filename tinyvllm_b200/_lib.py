@@ -32,6 +32,8 @@ SIGNATURES = {
     ),
     "tvk_selftest_umma_gemm": (_c_int, [_c_void] * 3 + [_c_int] * 5 + [_c_void, _c_void]),
     "tvk_paged_decode_attention_noalloc": (_c_int, [_c_void] * 6 + [_c_int] * 9 + [_c_void]),
+    "tvk_paged_decode_noalloc_status": (_c_int, [_c_void, _c_void]),
+    "tvk_debug_arm_wait_timeout": (_c_int, [ctypes.c_longlong]),
     "tvk_rms_norm": (_c_int, [_c_void] * 5 + [_c_int, _c_int, _c_float, _c_int, _c_void]),
     "tvk_rms_norm_write_kv": (_c_int, [_c_void] * 5 + [_c_int, _c_int, _c_float] + [_c_void] * 5 +
                               [_c_int] * 5 + [_c_void]),

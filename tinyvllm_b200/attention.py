@@ -40,18 +40,40 @@ def workspace_status(device: Optional[torch.device] = None, kind: str = "decode"
     return int(ws[:4].view(torch.int32).item())
 
 
+def status_word(device: Optional[torch.device] = None, kind: str = "decode") -> torch.Tensor:
+    """The current stream's workspace status word as a one-element int32 device tensor
+    (a view: a CUDA graph can copy it out alongside its results)."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    return _workspace(device, 0, kind)[:4].view(torch.int32)
+
+
+def check_workspace(device: Optional[torch.device] = None, kind: str = "decode", what: str = "kernel") -> None:
+    """Raise ``TvkError`` if a bounded wait inside a kernel that used the current
+    stream's ``kind`` workspace gave up (its output is then incomplete).  Reads the
+    status word (a device-to-host copy, so the stream is synchronised); on a
+    time-out the workspace header is zeroed first, so the next call starts clean."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    ws = _workspace(device, 0, kind)
+    if int(ws[:4].view(torch.int32).item()) != 0:
+        ws[:256].zero_()
+        raise _lib.TvkError(f"{what}: a bounded wait inside the kernel timed out; the output is incomplete")
+
+
 def paged_decode_attention(queries: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                            block_tables: torch.Tensor, context_lens: torch.Tensor,
                            n_heads: int, n_kv_heads: int, head_dim: int, block_size: int,
                            max_context_len: Optional[int] = None, *,
-                           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                           out: Optional[torch.Tensor] = None, check: bool = False) -> torch.Tensor:
     """Paged attention for decode (tinyvllm/model/llama.py:97-144).
 
     queries [B,1,Hq,D]; k_cache/v_cache [N,block_size,Hkv,D] (one layer's pool);
     block_tables int32 [B,max_blocks]; context_lens int32 [B].  Returns [B,1,Hq,D]
     in the pool dtype.  ``max_context_len=None`` attends over the whole table
     width masked by ``context_lens`` like the reference; an int truncates the
-    table to ``ceil(max_context_len / block_size)`` blocks first.
+    table to ``ceil(max_context_len / block_size)`` blocks first.  ``check=True``
+    synchronises the stream and raises ``TvkError`` if a bounded wait inside the
+    kernel timed out (the call is otherwise asynchronous; the engine checks once
+    per step instead).
     """
     dev = _lib.require_cuda(queries, k_cache, v_cache, block_tables, context_lens)
     B = queries.shape[0]
@@ -83,6 +105,8 @@ def paged_decode_attention(queries: torch.Tensor, k_cache: torch.Tensor, v_cache
         B, n_heads, n_kv_heads, head_dim, block_size, k_cache.shape[0], max_blocks, mcl,
         _lib.dtype_code(k_cache), ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
     _lib.check(rc, "tvk_paged_decode_attention")
+    if check:
+        check_workspace(dev, "decode", "tvk_paged_decode_attention")
     return out
 
 
@@ -91,7 +115,7 @@ def flash_prefill_attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Te
                                    slot_mapping: Optional[torch.Tensor] = None,
                                    k_cache: Optional[torch.Tensor] = None,
                                    v_cache: Optional[torch.Tensor] = None,
-                                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                                   out: Optional[torch.Tensor] = None, check: bool = False) -> torch.Tensor:
     """Causal (or full) attention over a ragged batch of prompts packed along tokens.
 
     q [T,Hq,D], k/v [T,Hkv,D]; ``cu_seqlens`` int32 [n+1] prefix sums of the prompt
@@ -99,7 +123,8 @@ def flash_prefill_attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Te
     (int64 [T], device; -1 skips a token) the kernel also writes each token's k/v
     row into ``k_cache/v_cache`` [N,block_size,Hkv,D] at flat slot
     ``block*block_size + offset`` -- the paged write of llama.py:188-209 fused
-    into the attention kernel.  Returns [T,Hq,D].
+    into the attention kernel.  Returns [T,Hq,D].  ``check=True`` synchronises and
+    raises ``TvkError`` if a bounded wait inside the kernel timed out.
     """
     tensors = [q, k, v, cu_seqlens] + [t for t in (slot_mapping, k_cache, v_cache) if t is not None]
     dev = _lib.require_cuda(*tensors)
@@ -136,6 +161,8 @@ def flash_prefill_attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Te
         Hq, Hkv, D, 1 if causal else 0, _lib.dtype_code(q), _lib.ptr(slot_mapping), _lib.ptr(k_cache),
         _lib.ptr(v_cache), num_blocks, block_size, ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
     _lib.check(rc, "tvk_flash_prefill_attention")
+    if check:
+        check_workspace(dev, "prefill", "tvk_flash_prefill_attention")
     return out
 
 

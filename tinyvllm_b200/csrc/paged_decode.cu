@@ -51,6 +51,8 @@ struct DecodeParams {
   int dynamic;         // 1: tc CTAs past their first unit take tickets from the workspace counter
   int max_splits;
   float scale_log2;  // log2(e) / sqrt(head_dim)
+  unsigned long long wait_ns;  // wall-time limit of every mbarrier wait
+  int drop_loads;              // wait-limit test: the producer issues nothing, so waits run out
 };
 
 __device__ __forceinline__ void report_timeout(int* status) {
@@ -310,11 +312,12 @@ __global__ void __launch_bounds__(160, 2)
       for (int it = 0; it < n_stage; ++it, ++it_g) {
         const int s = it_g % C::kStages;
         const uint32_t ph = (it_g / C::kStages) & 1;
-        if (!ptx::mbar_wait(&empty_bar[s], ph ^ 1)) {
+        if (!ptx::mbar_wait(&empty_bar[s], ph ^ 1, p.wait_ns)) {
           report_timeout(p.status);
           running = false;
           break;
         }
+        if (p.drop_loads) continue;  // test hook: nothing reaches the consumers
         if (!live || un.n_tok == 0) {
           // end of the list, or a sequence without context: no data
           if (lane == 0) {
@@ -378,7 +381,7 @@ __global__ void __launch_bounds__(160, 2)
   for (uint32_t it_g = 0;; ++it_g) {
     const int s = it_g % C::kStages;
     const uint32_t ph = (it_g / C::kStages) & 1;
-    if (!ptx::mbar_wait(&full_bar[s], ph)) {
+    if (!ptx::mbar_wait(&full_bar[s], ph, p.wait_ns)) {
       report_timeout(p.status);
       return;
     }
@@ -511,7 +514,7 @@ __global__ void __launch_bounds__(160, 2)
     // then when all have written this one.
     __syncwarp();
     if (lane == 0) ptx::mbar_arrive(&merge_bar[0]);
-    if (!ptx::mbar_wait(&merge_bar[0], n_merge & 1)) {
+    if (!ptx::mbar_wait(&merge_bar[0], n_merge & 1, p.wait_ns)) {
       report_timeout(p.status);
       return;
     }
@@ -535,7 +538,7 @@ __global__ void __launch_bounds__(160, 2)
     }
     __syncwarp();
     if (lane == 0) ptx::mbar_arrive(&merge_bar[1]);
-    if (!ptx::mbar_wait(&merge_bar[1], n_merge & 1)) {
+    if (!ptx::mbar_wait(&merge_bar[1], n_merge & 1, p.wait_ns)) {
       report_timeout(p.status);
       return;
     }
@@ -1005,6 +1008,9 @@ extern "C" int tvk_paged_decode_attention(const void* q, const void* k_cache, co
   p.split_tokens = plan.split;
   p.max_splits = plan.max_splits;
   p.scale_log2 = (float)(1.4426950408889634 / sqrt((double)head_dim));
+  const tvk::WaitTest wt = tvk::take_wait_test();
+  p.wait_ns = wt.armed ? wt.limit_ns : tvk::kDefaultWaitNs;
+  p.drop_loads = wt.armed && tc_shape ? 1 : 0;
 
   const size_t need = workspace_bytes_for(batch, n_heads, head_dim, p.max_splits);
   if (p.max_splits > 1) {
@@ -1107,4 +1113,21 @@ extern "C" int tvk_paged_decode_attention_noalloc(const void* q, const void* k_c
   return tvk_paged_decode_attention(q, k_cache, v_cache, block_tables, context_lens, out, batch, n_heads, n_kv_heads,
                                     head_dim, block_size, num_blocks, max_blocks, max_context_len, dtype, scratch,
                                     kNoAllocScratchBytes, stream);
+}
+
+// Status word of the no-allocation entry point's scratch on the current device
+// (byte 0 of the fixed array): waits for `stream`, then copies the word to the
+// host.  Non-zero means a bounded wait inside the last call's kernel gave up and
+// its output is incomplete.  The next no-allocation call clears the word.
+extern "C" int tvk_paged_decode_noalloc_status(int* status, void* stream) {
+  TVK_CHECK_ARG(status, "null status pointer");
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch_ptr(&scratch);
+  if (rc != TVK_OK) return rc;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int word = 0;
+  TVK_CHECK_CUDA(cudaMemcpyAsync(&word, scratch, sizeof(int), cudaMemcpyDeviceToHost, s));
+  TVK_CHECK_CUDA(cudaStreamSynchronize(s));
+  *status = word;
+  return TVK_OK;
 }

@@ -48,6 +48,8 @@ struct PrefillParams {
   int total_tokens;
   int sched_cap;                // tc path: entries the schedule can hold
   float scale_log2;
+  unsigned long long wait_ns;   // wall-time limit of every mbarrier wait
+  int drop_loads;               // wait-limit test: the producer loads nothing, so waits run out
 };
 
 __device__ __forceinline__ void report(int* status) {
@@ -260,7 +262,7 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
   uint32_t n_seen = 0;
   auto take_item = [&](Item& it, bool arrive) -> int {  // 1: item, 0: end of list, -1: gave up
     const int slot = n_seen % C::kItemSlots;
-    if (!wait_or_abort(&item_full[slot], (n_seen / C::kItemSlots) & 1, abort_flag)) return -1;
+    if (!wait_or_abort(&item_full[slot], (n_seen / C::kItemSlots) & 1, abort_flag, p.wait_ns)) return -1;
     volatile int* e = item_ring + slot * 8;
     it = Item{e[0], e[1], e[2], e[3], e[4]};
     if (arrive) ptx::mbar_arrive(&item_empty[slot]);
@@ -293,7 +295,7 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
           w = -1;
         }
       }
-      ok = __all_sync(0xffffffffu, wait_or_abort(&item_empty[slot], ((n_claim / C::kItemSlots) & 1) ^ 1, abort_flag));
+      ok = __all_sync(0xffffffffu, wait_or_abort(&item_empty[slot], ((n_claim / C::kItemSlots) & 1) ^ 1, abort_flag, p.wait_ns));
       if (!ok) break;
       if (lane == 0) {
         volatile int* e = item_ring + slot * 8;
@@ -306,10 +308,11 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
       }
       ++n_claim;
       if (w < 0) break;
+      if (p.drop_loads) break;  // test hook: the item's Q and K/V never arrive
       const int n_kv = kv_tiles(p, it);
       const int kvh = it.h / p.group;
       const int qs = q_it % C::kQSlots;
-      ok = __all_sync(0xffffffffu, wait_or_abort(&q_empty[qs], ((q_it / C::kQSlots) & 1) ^ 1, abort_flag));
+      ok = __all_sync(0xffffffffu, wait_or_abort(&q_empty[qs], ((q_it / C::kQSlots) & 1) ^ 1, abort_flag, p.wait_ns));
       if (!ok) break;
       if (lane == 0) {
         ptx::mbar_arrive_expect_tx(&q_full[qs], C::kQBytes);
@@ -322,7 +325,7 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
       for (int j = 0; j < n_kv; ++j, ++kv_it) {
         const int st = kv_it % S;
         const uint32_t ph = (kv_it / S) & 1;
-        ok = __all_sync(0xffffffffu, wait_or_abort(&kv_empty[st], ph ^ 1, abort_flag));
+        ok = __all_sync(0xffffffffu, wait_or_abort(&kv_empty[st], ph ^ 1, abort_flag, p.wait_ns));
         if (!ok) break;
         uint8_t* ks = base + C::kKOff + st * C::kKvBytes;
         uint8_t* vs = base + C::kVOff + st * C::kVStageBytes;
@@ -337,8 +340,8 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
         if (write_kv && (j >> 1) == it.mtile) {
           // The two diagonal tiles hold exactly this query tile's own tokens: copy
           // the landed rows into their paged slots (slot = block * block_size + offset).
-          ok = __all_sync(0xffffffffu, wait_or_abort(&k_full[st], ph, abort_flag) &&
-                                           wait_or_abort(&v_full[st], ph, abort_flag));
+          ok = __all_sync(0xffffffffu, wait_or_abort(&k_full[st], ph, abort_flag, p.wait_ns) &&
+                                           wait_or_abort(&v_full[st], ph, abort_flag, p.wait_ns));
           if (!ok) break;
           const int tok0 = it.s0 + j * 64, rows = min(64, it.L - j * 64);
           T* kc = reinterpret_cast<T*>(p.k_cache);
@@ -385,9 +388,9 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
       auto issue_pv = [&](uint32_t gg, bool first) -> bool {
         const int st = gg % S;
         const int pb = gg & 1;
-        if (!wait_or_abort(&p_full[pb], (gg >> 1) & 1, abort_flag)) return false;
-        if (first && !wait_or_abort(o_empty, (item_it & 1) ^ 1, abort_flag)) return false;
-        if (!wait_or_abort(&v_full[st], (gg / S) & 1, abort_flag)) return false;
+        if (!wait_or_abort(&p_full[pb], (gg >> 1) & 1, abort_flag, p.wait_ns)) return false;
+        if (first && !wait_or_abort(o_empty, (item_it & 1) ^ 1, abort_flag, p.wait_ns)) return false;
+        if (!wait_or_abort(&v_full[st], (gg / S) & 1, abort_flag, p.wait_ns)) return false;
         umma::fence_after_sync();
         const uint32_t v_addr = base_u32 + C::kVOff + st * C::kVStageBytes;
         const uint32_t lbo = D == 64 ? (uint32_t)(C::kOnesOff - (C::kVOff + st * C::kVStageBytes)) : C::kKvBlockBytes;
@@ -410,12 +413,12 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
         const int n_kv = kv_tiles(p, it);
         const int qs = q_it % C::kQSlots;
         const uint32_t q_addr = base_u32 + C::kQOff + qs * C::kQBytes;
-        ok = wait_or_abort(&q_full[qs], (q_it / C::kQSlots) & 1, abort_flag);
+        ok = wait_or_abort(&q_full[qs], (q_it / C::kQSlots) & 1, abort_flag, p.wait_ns);
         for (int j = 0; ok && j < n_kv; ++j, ++g) {
           const int st = g % S;
           const int sb = g & 1;
-          ok = wait_or_abort(&k_full[st], (g / S) & 1, abort_flag) &&
-               wait_or_abort(&pv_done[sb], ((g >> 1) & 1) ^ 1, abort_flag);
+          ok = wait_or_abort(&k_full[st], (g / S) & 1, abort_flag, p.wait_ns) &&
+               wait_or_abort(&pv_done[sb], ((g >> 1) & 1) ^ 1, abort_flag, p.wait_ns);
           if (!ok) break;
           umma::fence_after_sync();
           const uint32_t k_addr = base_u32 + C::kKOff + st * C::kKvBytes;
@@ -452,7 +455,7 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
     Item it;
     // wait until O += P(gg).V(gg) has completed
     auto wait_pv = [&](uint32_t gg) -> bool {
-      return __all_sync(0xffffffffu, wait_or_abort(&pv_done[gg & 1], (gg >> 1) & 1, abort_flag));
+      return __all_sync(0xffffffffu, wait_or_abort(&pv_done[gg & 1], (gg >> 1) & 1, abort_flag, p.wait_ns));
     };
     while (ok) {
       int got = take_item(it, false);
@@ -467,7 +470,7 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
       float m = -INFINITY;  // running max (log2 domain) that P and O are scaled by
       for (int j = 0; j < n_kv; ++j, ++g) {
         const int sb = g & 1;
-        ok = __all_sync(0xffffffffu, wait_or_abort(&s_full[sb], (g >> 1) & 1, abort_flag));
+        ok = __all_sync(0xffffffffu, wait_or_abort(&s_full[sb], (g >> 1) & 1, abort_flag, p.wait_ns));
         if (!ok) break;
         umma::fence_after_sync();
         float s[64];
@@ -844,6 +847,9 @@ extern "C" int tvk_flash_prefill_attention(const void* q, const void* k, const v
   p.scale_log2 = (float)(1.4426950408889634 / sqrt((double)head_dim));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const bool tc = dtype != TVK_DTYPE_F32 && (head_dim == 64 || head_dim == 128);
+  const tvk::WaitTest wt = tvk::take_wait_test();
+  p.wait_ns = wt.armed ? wt.limit_ns : tvk::kDefaultWaitNs;
+  p.drop_loads = wt.armed && tc ? 1 : 0;
   if (tc) {
     if (p.n_mtiles > kMaxBands) {
       tvk::set_error("max_seqlen %d exceeds the %d-token limit of the tcgen05 path", max_seqlen, kMaxBands * 128);

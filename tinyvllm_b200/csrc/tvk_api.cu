@@ -29,8 +29,25 @@ EncodeTiledFn encode_tiled_fn() {
   return fn;
 }
 
+static thread_local WaitTest g_wait_test = {false, 0};
+
+WaitTest take_wait_test() {
+  const WaitTest w = g_wait_test;
+  g_wait_test = WaitTest{false, 0};
+  return w;
+}
+
 }  // namespace tvk
 
 extern "C" int tvk_abi_version(void) { return 1; }
+
+extern "C" int tvk_debug_arm_wait_timeout(long long limit_ns) {
+  if (limit_ns < 100000 || limit_ns > (long long)tvk::kDefaultWaitNs) {
+    tvk::set_error("wait limit %lld ns outside [1e5, 2e9]", limit_ns);
+    return TVK_ERR_INVALID;
+  }
+  tvk::g_wait_test = tvk::WaitTest{true, (unsigned long long)limit_ns};
+  return TVK_OK;
+}
 
 extern "C" const char* tvk_last_error(void) { return tvk::g_last_error; }

@@ -56,6 +56,19 @@ EncodeTiledFn encode_tiled_fn();
 constexpr int kWorkspaceHeader = 256;
 constexpr int kStatusWaitTimeout = 1;
 
+// Wall-time limit of every mbarrier wait in the decode and prefill kernels.
+constexpr unsigned long long kDefaultWaitNs = 2000000000ull;
+
+// Wait-limit test hook (tvk_debug_arm_wait_timeout): when armed, the next
+// decode or prefill launch on the calling thread gets `limit_ns` as its wait
+// limit and a flag telling its producer warp to issue no loads, so the first
+// consumer wait runs out of time.  Reading it disarms it.
+struct WaitTest {
+  bool armed;
+  unsigned long long limit_ns;
+};
+WaitTest take_wait_test();
+
 }  // namespace tvk
 
 // ----------------------------------------------------------------------------

@@ -33,6 +33,7 @@ import numpy as np
 import torch
 
 from . import layers
+from .attention import check_workspace
 from .block_manager import BlockManager
 from .model import KVCache, Llama
 
@@ -327,10 +328,12 @@ class LLMEngine:
         logits = self.model.prefill(torch.from_numpy(toks).to(dev), torch.from_numpy(pos).to(dev),
                                     torch.from_numpy(cu).to(dev), max(lens), torch.from_numpy(slots).to(dev),
                                     self.kv_cache)
+        sampled = self._sample(logits, seqs)
+        check_workspace(dev, "prefill", "prefill step")     # a kernel wait that timed out raises here
         for s, L in zip(seqs, lens):
             bm.advance_position(s.seq_id, L)
         self.stats["prefill_tokens"] += int(sum(lens))
-        return self._sample(logits, seqs)
+        return sampled
 
     def _decode(self, seqs: List[Sequence]) -> List[int]:
         bm = self.block_manager
@@ -368,11 +371,14 @@ class LLMEngine:
                                        torch.from_numpy(ctx).to(dev), torch.from_numpy(slots).to(dev),
                                        self.kv_cache, self.kv_order)
             sampled = None
+        if sampled is None:
+            sampled = self._sample(logits, seqs)
+            check_workspace(self.device, "decode", "decode step")
         for i in ids:
             bm.advance_position(i)
         self.stats["decode_tokens"] += len(seqs)
         self.stats["decode_steps"] += 1
-        return sampled if sampled is not None else self._sample(logits, seqs)
+        return sampled
 
     def _sample(self, logits: torch.Tensor, seqs: List[Sequence]) -> List[int]:
         """Greedy pick for each row of ``logits`` [len(seqs), vocab] (sampling.py:133-134)."""

@@ -28,8 +28,8 @@ from typing import Dict, List, Optional, Sequence
 import numpy as np
 import torch
 
-from . import layers
-from .attention import flash_prefill_attention_varlen, paged_decode_attention
+from . import _lib, layers
+from .attention import flash_prefill_attention_varlen, paged_decode_attention, status_word
 
 _DTYPES = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}
 
@@ -253,6 +253,10 @@ class DecodeGraph:
 
     Rows beyond the live batch are padding: token 0, context 1 over block 0,
     slot -1 (no K/V write), and their outputs are ignored.
+
+    The graph also copies the decode workspace's status word out with the
+    tokens; ``run`` raises ``TvkError`` if a bounded wait inside an attention
+    kernel of the step timed out.
     """
 
     def __init__(self, model: Llama, batch: int, table_width: int, kv_cache: KVCache, kv_order: str):
@@ -263,14 +267,14 @@ class DecodeGraph:
         self.bt = torch.zeros(batch, table_width, dtype=torch.int32, device=dev)
         self.ctx = torch.ones(batch, dtype=torch.int32, device=dev)
         self.slots = torch.full((batch,), -1, dtype=torch.int64, device=dev)
-        self.out = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.out = torch.zeros(batch + 1, dtype=torch.int32, device=dev)   # tokens, then the status word
         # pinned staging for the per-step host -> device copies
         self.h_tok = torch.zeros(batch, dtype=torch.int32).pin_memory()
         self.h_pos = torch.zeros(batch, dtype=torch.int32).pin_memory()
         self.h_bt = torch.zeros(batch, table_width, dtype=torch.int32).pin_memory()
         self.h_ctx = torch.ones(batch, dtype=torch.int32).pin_memory()
         self.h_slots = torch.full((batch,), -1, dtype=torch.int64).pin_memory()
-        self.h_out = torch.zeros(batch, dtype=torch.int32).pin_memory()
+        self.h_out = torch.zeros(batch + 1, dtype=torch.int32).pin_memory()
         self.stream = torch.cuda.Stream(dev)
         self.stream.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(self.stream):
@@ -284,7 +288,11 @@ class DecodeGraph:
 
     def _forward(self):
         logits = self.model.decode(self.tok, self.pos, self.bt, self.ctx, self.slots, self.kv_cache, self.kv_order)
-        layers.greedy_argmax(logits, out=self.out)
+        layers.greedy_argmax(logits, out=self.out[:self.batch])
+        # the attention calls of this step used this stream's workspace; the view
+        # also keeps that workspace alive for as long as the graph exists
+        self._status = status_word(self.model.device, "decode")
+        self.out[self.batch:].copy_(self._status)
 
     def run(self, tokens: np.ndarray, positions: np.ndarray, tables: np.ndarray, ctx: np.ndarray,
             slots: np.ndarray) -> np.ndarray:
@@ -308,4 +316,10 @@ class DecodeGraph:
             self.h_out.copy_(self.out, non_blocking=True)
         self.stream.synchronize()
         cur.wait_stream(self.stream)
+        if int(self.h_out[self.batch]) != 0:
+            with torch.cuda.stream(self.stream):
+                self._status.zero_()
+            self.stream.synchronize()
+            raise _lib.TvkError("decode step: a bounded wait inside an attention kernel timed out; "
+                                "the step's tokens are not valid")
         return self.h_out.numpy()[:n].copy()
