@@ -1,24 +1,36 @@
-"""Benchmark of the paged-decode attention hot path on B200.
+"""Benchmark of the tinyvllm attention hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (config 3 of the hot-path contract): one paged-decode attention call
-over 256 sequences per GPU, 32 query / 8 KV heads, head_dim 128, block 16,
-fp16 K/V, contexts ~ U{128..4096}, random non-contiguous tables in a pool
-1.2x the blocks needed.  A *step* is one such call (one attention layer of one
-decode step).  ``value`` = decode tokens (sequences) attended per second,
-summed over all GPUs.  Each rank holds its own independently seeded batch
-(weak scaling, no data-path collective).  Every step reads ~2.2 GB of K/V per
-GPU, far larger than the 126 MB L2, so no flush is needed between steps.
+Headline workload (config 3 of the hot-path contract), per GPU: one decode
+step of the attention layer over 256 sequences, 32 query / 8 KV heads,
+head_dim 128, block 16, fp16 K/V, contexts ~ U{128..4096}, random
+non-contiguous tables in a pool 1.2x the blocks needed; then, as the
+sequence-sharded engine does every step, the greedy pick over a per-rank
+[256, vocab 128256] logits buffer and the NCCL all-gather of the int32 tokens
+over all ranks.  A *step* is that attention call + argmax + token all-gather.
+``value`` = decode tokens (sequences) per second, summed over all GPUs.  Each
+rank holds its own independently seeded batch (weak scaling); the all-gather
+is the only exchange.  Every step reads ~2.2 GB of K/V per GPU, far larger
+than the 126 MB L2, so no flush is needed between steps.
 
-``e2e`` times the same call through the public Python API with the per-step
-inputs (queries, block tables, context lengths) copied from pinned host
-memory and the output copied back inside the timed region; the KV pool is
+``roofline`` covers the attention call alone (its own CUDA events).  ``e2e``
+times the same step through the public Python API with the per-step inputs
+(queries, block tables, context lengths) copied from pinned host memory and
+the gathered tokens copied back inside the timed region; the KV pool is
 device-resident state, as it is in the reference engine.
 
+The same JSON line nests the other configurations' results (``--no-nested``
+skips them): ``prefill`` (config 2, one ragged causal prefill call with the
+paged K/V write), ``engine_config4`` (TinyLlama-1.1B fp16 under continuous
+batching, N=1 only) and ``engine_config5`` (Llama-3-8B-shape bf16 decode,
+512 sequences sharded by sequence over the N ranks with the per-step token
+all-gather).
+
 ``--impl reference`` times the reference algorithm on the host cores: the
-numpy restatement of tinyvllm/model/llama.py:97-144 (tinygrad itself is not
-installable in this image), on a bounded sample of the same workload.
+numpy restatement of tinyvllm/model/llama.py:97-144 plus the greedy pick
+(tinygrad itself is not installable in this image), on a bounded sample of
+the same workload.
 """
 
 from __future__ import annotations
@@ -37,9 +49,11 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-METRIC = "paged-decode attention: decode tok/s (one attention-layer call over the batch per step)"
+METRIC = ("decode tok/s: one paged-decode attention layer over the batch + greedy pick + int32 token "
+          "all-gather across ranks per step")
 UNIT = "tok/s"
 CPU_SAMPLE_SEQS = 16
+VOCAB = 128256     # Llama-3-8B vocabulary (config 3 has its attention layout)
 
 
 def _peaks():
@@ -152,8 +166,10 @@ def _fastest_blas_threads(call) -> int:
 
 
 def cpu_baseline_sample(n_seqs: int = CPU_SAMPLE_SEQS, reps: int = 5):
-    """Time the oracle restatement of the reference path on a bounded sample of
-    config 3: the first ``n_seqs`` sequences with their own blocks, on the host."""
+    """Time the oracle restatement of the reference step on a bounded sample of
+    config 3: the first ``n_seqs`` sequences with their own blocks (attention,
+    llama.py:97-144) plus the greedy pick over their [n_seqs, vocab] logits
+    (sampling.py:133-134), on the host."""
     import numpy as np
     from oracle import attention as oa
     from tinyvllm_b200 import workloads
@@ -163,18 +179,24 @@ def cpu_baseline_sample(n_seqs: int = CPU_SAMPLE_SEQS, reps: int = 5):
     vc = case.v_cache.float().numpy()
     bt = case.block_tables.numpy()
     ctx = case.context_lens.numpy()
-    threads = _fastest_blas_threads(lambda: oa.paged_decode_attention(q, kc, vc, bt, ctx, 32, 8, 128, 16))
+    logits = np.random.default_rng(4321).standard_normal((n_seqs, VOCAB), dtype=np.float32)
+
+    def one():
+        oa.paged_decode_attention(q, kc, vc, bt, ctx, 32, 8, 128, 16)
+        oa.greedy_argmax(logits)
+
+    threads = _fastest_blas_threads(one)
     times = []
     for _ in range(reps):
         t0 = time.perf_counter()
-        oa.paged_decode_attention(q, kc, vc, bt, ctx, 32, 8, 128, 16)
+        one()
         times.append(time.perf_counter() - t0)
     med = statistics.median(times)
-    cores = threads
     sample = (f"first {n_seqs} sequences of config 3 (ctx sum {int(ctx.sum())}, table width "
-              f"{bt.shape[1]} blocks), numpy restatement of llama.py:97-144, median of {reps}, "
-              f"{threads} BLAS thread(s), the faster of one and all host cores")
-    return {"value": n_seqs / med, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
+              f"{bt.shape[1]} blocks) + argmax over [{n_seqs}, {VOCAB}] logits, numpy restatement of "
+              f"llama.py:97-144 and sampling.py:133-134, median of {reps}, {threads} BLAS thread(s), the "
+              "faster of one and all host cores")
+    return {"value": n_seqs / med, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample,
             "seconds_per_call": med}
 
 
@@ -191,56 +213,91 @@ def run_reference(args, rank: int, world: int) -> int:
     vc = case.v_cache.float().numpy()
     bt = case.block_tables.numpy()
     ctx = case.context_lens.numpy()
-    threads = _fastest_blas_threads(lambda: oa.paged_decode_attention(q, kc, vc, bt, ctx, 32, 8, 128, 16))
-    for _ in range(args.warmup):
+    logits = np.random.default_rng(4321).standard_normal((n, VOCAB), dtype=np.float32)
+
+    def one():
         oa.paged_decode_attention(q, kc, vc, bt, ctx, 32, 8, 128, 16)
+        oa.greedy_argmax(logits)
+
+    threads = _fastest_blas_threads(one)
+    for _ in range(args.warmup):
+        one()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        oa.paged_decode_attention(q, kc, vc, bt, ctx, 32, 8, 128, 16)
+        one()
     dt = (time.perf_counter() - t0) / args.steps
     value = n / dt
-    cores = threads
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config3 paged decode, bounded sample", "batch": n, "n_heads": 32,
-                   "n_kv_heads": 8, "head_dim": 128, "block_size": 16, "ctx": "U{128..4096}"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+        "config": {"workload": "config3 paged decode + greedy pick, bounded sample", "batch": n, "n_heads": 32,
+                   "n_kv_heads": 8, "head_dim": 128, "block_size": 16, "ctx": "U{128..4096}", "vocab": VOCAB},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                          "sample": f"first {n} sequences of config 3 per step; tinygrad absent, so the numpy "
-                                   f"restatement of llama.py:97-144 on {threads} BLAS thread(s), the faster "
-                                   "of one and all host cores"},
+                                   f"restatement of llama.py:97-144 and sampling.py:133-134 on {threads} BLAS "
+                                   "thread(s), the faster of one and all host cores"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
-def run_ours(args, rank: int, world: int, local_rank: int) -> int:
+def _free_port() -> int:
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _init_group(rank: int, world: int, dev) -> None:
+    """One NCCL process group for the whole run (a one-rank group at N=1, so the
+    step's token all-gather runs at every N).  Short timeout: ranks that wait for
+    one another end with an error instead of hanging."""
+    import datetime
+    import torch.distributed as dist
+    if dist.is_initialized():
+        return
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    if "MASTER_PORT" not in os.environ:
+        os.environ["MASTER_PORT"] = str(_free_port())
+    dist.init_process_group("nccl", device_id=dev, rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+
+
+def decode_headline(args, rank: int, world: int, local_rank: int):
+    """Config 3 per rank: attention + greedy pick + token all-gather per step."""
     import torch
     import torch.distributed as dist
-    from tinyvllm_b200 import workloads
+    from tinyvllm_b200 import layers, workloads
     from tinyvllm_b200.attention import paged_decode_attention
 
-    torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
-
     case = workloads.decode_config3(dev, batch=args.batch, seed_offset=rank)
     B = case.batch
-    args_call = (case.q, case.k_cache, case.v_cache, case.block_tables, case.context_lens, 32, 8, 128, 16)
-    out = torch.empty_like(case.q)
+    g = torch.Generator(device=dev).manual_seed(4321 + rank)
+    logits = torch.randn(B, VOCAB, generator=g, device=dev, dtype=torch.float32).half()
     stream = torch.cuda.current_stream(dev)
 
+    def step(q, bt, ctx, o, tokens, gathered, ev=None):
+        if ev is not None:
+            ev[0].record(stream)
+        paged_decode_attention(q, case.k_cache, case.v_cache, bt, ctx, 32, 8, 128, 16, out=o)
+        if ev is not None:
+            ev[1].record(stream)
+        layers.greedy_argmax(logits, out=tokens)
+        dist.all_gather_into_tensor(gathered, tokens)
+
+    out = torch.empty_like(case.q)
+    tokens = torch.empty(B, dtype=torch.int32, device=dev)
+    gathered = torch.empty(world * B, dtype=torch.int32, device=dev)
+
     def barrier():
-        if world > 1:
-            dist.barrier(device_ids=[local_rank])
+        dist.barrier(device_ids=[local_rank])
         torch.cuda.synchronize(dev)
 
     for _ in range(args.warmup):
-        paged_decode_attention(*args_call, out=out)
+        step(case.q, case.block_tables, case.context_lens, out, tokens, gathered)
     barrier()
 
     clocks = ClockSampler(world) if rank == 0 else None
@@ -254,25 +311,23 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record(stream)
     for i in range(args.steps):
-        ev[i][0].record(stream)
-        paged_decode_attention(*args_call, out=out)
-        ev[i][1].record(stream)
+        step(case.q, case.block_tables, case.context_lens, out, tokens, gathered, ev[i])
     t_end.record(stream)
     barrier()
     total_ms = t_start.elapsed_time(t_end)
-    per_step = [a.elapsed_time(b) for a, b in ev]
+    per_attn = [a.elapsed_time(b) for a, b in ev]
 
     # ---- end-to-end through the public API with host buffers ----
-    # Every step copies its inputs from pinned host memory and its output back.
-    # The copies run on their own streams into two alternating sets of device
-    # buffers, so the transfers of neighbouring steps overlap this step's kernel
-    # (as a serving loop overlaps them); events order each slot's reuse.
+    # Every step copies its inputs from pinned host memory and the gathered tokens
+    # back.  The copies run on their own streams into two alternating sets of
+    # device buffers, so the transfers of neighbouring steps overlap this step's
+    # kernels (as a serving loop overlaps them); events order each slot's reuse.
     q_h = case.q.cpu().pin_memory()
     bt_h = case.block_tables.cpu().pin_memory()
     ctx_h = case.context_lens.cpu().pin_memory()
-    out_h = torch.empty(case.q.shape, dtype=case.q.dtype).pin_memory()
+    tok_h = torch.empty(world * B, dtype=torch.int32).pin_memory()
     bufs = [(torch.empty_like(case.q), torch.empty_like(case.block_tables), torch.empty_like(case.context_lens),
-             torch.empty_like(case.q)) for _ in range(2)]
+             torch.empty_like(case.q), torch.empty_like(tokens), torch.empty_like(gathered)) for _ in range(2)]
     h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     ev_in = [torch.cuda.Event() for _ in range(2)]
     ev_done = [torch.cuda.Event() for _ in range(2)]
@@ -283,22 +338,22 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
         i = n_issued[0]
         n_issued[0] += 1
         sl = i % 2
-        q_d, bt_d, ctx_d, o_d = bufs[sl]
+        q_d, bt_d, ctx_d, o_d, t_d, g_d = bufs[sl]
         with torch.cuda.stream(h2d):
             if i >= 2:
-                h2d.wait_event(ev_done[sl])          # step i-2's kernel has read this slot
+                h2d.wait_event(ev_done[sl])          # step i-2's kernels have read this slot
             q_d.copy_(q_h, non_blocking=True)
             bt_d.copy_(bt_h, non_blocking=True)
             ctx_d.copy_(ctx_h, non_blocking=True)
             ev_in[sl].record(h2d)
         stream.wait_event(ev_in[sl])
         if i >= 2:
-            stream.wait_event(ev_out[sl])            # step i-2's output has left this slot
-        paged_decode_attention(q_d, case.k_cache, case.v_cache, bt_d, ctx_d, 32, 8, 128, 16, out=o_d)
+            stream.wait_event(ev_out[sl])            # step i-2's tokens have left this slot
+        step(q_d, bt_d, ctx_d, o_d, t_d, g_d)
         ev_done[sl].record(stream)
         with torch.cuda.stream(d2h):
             d2h.wait_event(ev_done[sl])
-            out_h.copy_(o_d, non_blocking=True)
+            tok_h.copy_(g_d, non_blocking=True)
             ev_out[sl].record(d2h)
 
     for _ in range(3):
@@ -315,8 +370,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
     torch.cuda.synchronize(dev)
     barrier()
     e2e_ms = e0.elapsed_time(e1)
-    # the same steps with every copy and the kernel in one stream, for reference
-    q_d, bt_d, ctx_d, o_d = bufs[0]
+    # the same steps with every copy and kernel in one stream, for reference
+    q_d, bt_d, ctx_d, o_d, t_d, g_d = bufs[0]
     s0 = torch.cuda.Event(enable_timing=True)
     s1 = torch.cuda.Event(enable_timing=True)
     s0.record(stream)
@@ -324,71 +379,70 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
         q_d.copy_(q_h, non_blocking=True)
         bt_d.copy_(bt_h, non_blocking=True)
         ctx_d.copy_(ctx_h, non_blocking=True)
-        paged_decode_attention(q_d, case.k_cache, case.v_cache, bt_d, ctx_d, 32, 8, 128, 16, out=o_d)
-        out_h.copy_(o_d, non_blocking=True)
+        step(q_d, bt_d, ctx_d, o_d, t_d, g_d)
+        tok_h.copy_(g_d, non_blocking=True)
     s1.record(stream)
     torch.cuda.synchronize(dev)
     serial_ms = s0.elapsed_time(s1)
+    barrier()
     clk = clocks.stop() if clocks else None
 
     # max over ranks
     t = torch.tensor([total_ms, e2e_ms, serial_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
     total_ms, e2e_ms, serial_ms = float(t[0]), float(t[1]), float(t[2])
-
-    if rank == 0:
-        from tinyvllm_b200 import _lib
-        ms = total_ms / args.steps
-        value = B * world * args.steps / (total_ms / 1e3)
-        e2e_value = B * world * args.steps / (e2e_ms / 1e3)
-        peak, peak_kind = _peaks()
-        alg = case.algorithmic_bytes()
-        avg_launch_ms = statistics.mean(per_step)
-        achieved = alg / (avg_launch_ms / 1e3) / 1e9
-        L = _lib.lib()
-        plan = (ctypes.c_int * 4)()
-        _lib.check(L.tvk_paged_decode_plan(B, 32, 8, 128, 16, case.block_tables.shape[1], -1, 1, plan),
-                   "tvk_paged_decode_plan")
-        launches_per_step = plan[2]
-        traffic_path = ROOT / "profiles" / "paged_decode_tc_config3.traffic.json"
-        traffic = None
-        if traffic_path.exists():
-            traffic = json.loads(traffic_path.read_text()).get("bytes_per_launch")
-        cpu = cpu_baseline_sample() if world == 1 and not args.no_cpu_baseline else None
-        h2d_bytes = q_h.numel() * q_h.element_size() + bt_h.numel() * 4 + ctx_h.numel() * 4
-        d2h_bytes = out_h.numel() * out_h.element_size()
-        line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": "config3 paged-decode attention (256 seqs/GPU, 32q/8kv heads, D=128, "
-                                   "block 16, fp16, ctx U{128..4096}, shuffled tables, pool 1.2x)",
-                       "batch_per_gpu": B, "global_batch": B * world, "ctx_sum_rank0": int(case.context_lens.sum()),
-                       "l2": "no flush: each step reads ~2.2 GB of K/V per GPU (> 126 MB L2)",
-                       "parallelism": f"sequence-sharded x{world}, no data-path collective"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
-                         "algorithmic_bytes_per_launch": alg,
-                         "avg_step_ms": avg_launch_ms,
-                         "note": "per-step events bracket the whole call (main kernel, plus the split-K combine when the plan has one)",
-                         "unit_tokens": plan[0], "max_splits": plan[1], "persistent": bool(plan[3])},
-            "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
-                    "ms_per_step": e2e_ms / args.steps,
-                    "overlap": "copies on two extra streams, double-buffered: step i+1's inputs and step i-1's "
-                               "output move while step i's kernel runs",
-                    "serial": {"value": B * world * args.steps / (serial_ms / 1e3),
-                               "ms_per_step": serial_ms / args.steps,
-                               "note": "copies and kernel in one stream, nothing overlapped"}},
-            "clocks": clk,
-            "gpu_launches": launches_per_step * args.steps,
-        }
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier(device_ids=[local_rank])
-        dist.destroy_process_group()
-    return 0
+    if rank != 0:
+        return None
+    from tinyvllm_b200 import _lib
+    ms = total_ms / args.steps
+    value = B * world * args.steps / (total_ms / 1e3)
+    e2e_value = B * world * args.steps / (e2e_ms / 1e3)
+    peak, peak_kind = _peaks()
+    alg = case.algorithmic_bytes()
+    avg_attn_ms = statistics.mean(per_attn)
+    achieved = alg / (avg_attn_ms / 1e3) / 1e9
+    L = _lib.lib()
+    plan = (ctypes.c_int * 4)()
+    _lib.check(L.tvk_paged_decode_plan(B, 32, 8, 128, 16, case.block_tables.shape[1], -1, 1, plan),
+               "tvk_paged_decode_plan")
+    traffic_path = ROOT / "profiles" / "paged_decode_tc_config3.traffic.json"
+    traffic = None
+    if traffic_path.exists():
+        traffic = json.loads(traffic_path.read_text()).get("bytes_per_launch")
+    cpu = cpu_baseline_sample() if world == 1 and not args.no_cpu_baseline else None
+    h2d_bytes = q_h.numel() * q_h.element_size() + bt_h.numel() * 4 + ctx_h.numel() * 4
+    d2h_bytes = tok_h.numel() * 4
+    return {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "config3 paged-decode attention (256 seqs/GPU, 32q/8kv heads, D=128, "
+                               "block 16, fp16, ctx U{128..4096}, shuffled tables, pool 1.2x) + greedy pick over "
+                               f"[256, {VOCAB}] fp16 logits + NCCL all-gather of the int32 tokens",
+                   "batch_per_gpu": B, "global_batch": B * world, "ctx_sum_rank0": int(case.context_lens.sum()),
+                   "l2": "no flush: each step reads ~2.2 GB of K/V per GPU (> 126 MB L2)",
+                   "parallelism": f"sequence-sharded x{world}; per step one all-gather of {B} int32 tokens per rank"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_launch": alg,
+                     "avg_attention_ms": avg_attn_ms,
+                     "note": "the attention call's own CUDA events (main kernel, plus the split-K combine when "
+                             "the plan has one); the step adds the argmax and the all-gather",
+                     "unit_tokens": plan[0], "max_splits": plan[1], "persistent": bool(plan[3])},
+        "step_breakdown_ms": {"attention": avg_attn_ms, "argmax_and_all_gather": ms - avg_attn_ms},
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": d2h_bytes,
+                "ms_per_step": e2e_ms / args.steps,
+                "overlap": "copies on two extra streams, double-buffered: step i+1's inputs and step i-1's "
+                           "tokens move while step i's kernels run",
+                "serial": {"value": B * world * args.steps / (serial_ms / 1e3),
+                           "ms_per_step": serial_ms / args.steps,
+                           "note": "copies and kernels in one stream, nothing overlapped"}},
+        "clocks": clk,
+        "gpu_launches": (plan[2] + 1) * args.steps,
+        "gpu_launches_note": "per step: the attention kernel(s) and the argmax kernel; NCCL's own kernel "
+                             "for the all-gather is not counted",
+    }
 
 
 PREFILL_LENS = (1, 15, 16, 17, 128, 500, 1024, 2048)
@@ -402,7 +456,7 @@ def _tensor_peak():
     return 1590.0, "fallback"
 
 
-def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
+def prefill_line(args, rank: int, world: int, local_rank: int):
     """Config 2: 8 fp16 prompts (32q/4kv heads, D=64) through one ragged causal
     prefill call with the paged K/V write into a fresh 1024-block pool."""
     import numpy as np
@@ -410,7 +464,6 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
     from tinyvllm_b200.attention import flash_prefill_attention_varlen
     from tinyvllm_b200.block_manager import BlockManager
 
-    torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     lens = tuple(int(x) for x in args.prefill_lens.split(",")) if args.prefill_lens else PREFILL_LENS
     hq, hkv, hd = 32, args.prefill_kv_heads, args.prefill_head_dim
@@ -434,6 +487,7 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
     out = torch.empty_like(q)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)   # > 126 MB L2
     stream = torch.cuda.current_stream(dev)
+    steps = args.prefill_steps
 
     def call():
         flash_prefill_attention_varlen(q, k, v, cu, max(lens), True, slot_mapping=slots, k_cache=kc, v_cache=vc,
@@ -443,8 +497,8 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
         call()
     torch.cuda.synchronize(dev)
     # The device-resident number replays the call from a CUDA graph, so the host's
-    # launch work (argument checks, tensor-map encoding; ~25 us) does not leave
-    # the GPU idle inside the events; the e2e number below keeps it.
+    # launch work (argument checks, tensor-map encoding) does not leave the GPU
+    # idle inside the events; the e2e number below keeps it.
     side = torch.cuda.Stream(dev)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.stream(side):
@@ -456,12 +510,12 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
     for _ in range(args.warmup):
         graph.replay()
     torch.cuda.synchronize(dev)
-    clocks = ClockSampler(world) if rank == 0 else None
+    clocks = ClockSampler(1) if rank == 0 else None
     if clocks:
         clocks.start()
         time.sleep(0.3)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    for i in range(args.steps):
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
         # Evict q/k/v from L2 between steps (not timed): write a buffer larger than
         # L2, then read it back so that the dirty lines are written out here and
         # not inside the next timed call.
@@ -492,23 +546,23 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(steps):
         e2e_step()
     e1.record(stream)
     torch.cuda.synchronize(dev)
-    e2e_ms = e0.elapsed_time(e1) / args.steps
+    e2e_ms = e0.elapsed_time(e1) / steps
     h2d = sum(t.numel() * t.element_size() for t in (q_h, k_h, v_h, cu_h, slots_h))
     d2h = out_h.numel() * out_h.element_size()
     clk = clocks.stop() if clocks else None
     del graph
     if rank != 0:
-        return 0
+        return None
     ms = statistics.mean(per_step)
     flops = 4.0 * hq * hd * sum(L * (L + 1) / 2 for L in lens)
     achieved = flops / (ms / 1e3) / 1e12
     peak, kind = _tensor_peak()
     cpu = None
-    if not args.no_cpu_baseline and is_cfg2:
+    if not args.no_cpu_baseline and is_cfg2 and world == 1:
         from oracle import attention as oa
         threads = _all_host_threads()
         qn, kn, vn = q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy()
@@ -516,13 +570,18 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
         for i, L in enumerate(lens):
             a, b = int(cu[i]), int(cu[i + 1])
             oa.flash_prefill_attention(qn[None, a:b], kn[None, a:b], vn[None, a:b], True)
-        dt = time.perf_counter() - t0
-        cpu = {"value": T / dt, "unit": "prompt tok/s", "cores": threads, "kind": "port",
+        dt_cpu = time.perf_counter() - t0
+        cpu = {"value": T / dt_cpu, "unit": "prompt tok/s", "cores": threads, "kind": "port",
                "sample": "all 8 config-2 prompts once, numpy restatement of llama.py:58-94"}
-    line = {
+    traffic = None
+    tp = ROOT / "profiles" / "flash_prefill_tc_config2.traffic.json"
+    if is_cfg2 and tp.exists():
+        traffic = json.loads(tp.read_text()).get("bytes_per_launch")
+    exp_bound = 2.0 * 2 * 128 * 64 * hd / 512 * 148 * 1.965e9 / 1e12
+    return {
         "metric": "flash-prefill attention: prompt tok/s (" + ("config 2" if is_cfg2 else "custom prompts") +
                   ", one ragged call per step)",
-        "value": T / (ms / 1e3), "unit": "prompt tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "value": T / (ms / 1e3), "unit": "prompt tok/s", "n_gpus": 1, "steps": steps, "warmup": args.warmup,
         "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16" if dt == torch.bfloat16 else "f16",
         "data": "synthetic",
@@ -530,21 +589,19 @@ def run_prefill(args, rank: int, world: int, local_rank: int) -> int:
                                ",".join(map(str, lens)) + f", {hq}q/{hkv}kv heads, D={hd}, " +
                                ("bf16" if dt == torch.bfloat16 else "fp16") + f", paged write into {n_blocks} blocks",
                    "l2": "flushed between steps (256 MB write, then read back; outside the events)",
-                   "timing": "CUDA-graph replay of the call (schedule + attention kernels) between events"},
+                   "timing": "CUDA-graph replay of the call between events"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak, "traffic": None, "peak_kind": kind,
+                     "frac": achieved / peak, "traffic": traffic, "peak_kind": kind,
                      "algorithmic_flops_per_launch": flops,
                      # a 128x64 tile needs 8192 exponentials (512 cycles of the 16/cycle
                      # MUFU unit) for 2 * 2 * 128 * 64 * head_dim FLOP of MMA work
-                     "exp_unit_bound_tflops": 2.0 * 2 * 128 * 64 * hd / 512 * 148 * 1.965e9 / 1e12,
-                     "frac_of_exp_unit_bound": achieved / (2.0 * 2 * 128 * 64 * hd / 512 * 148 * 1.965e9 / 1e12)},
+                     "exp_unit_bound_tflops": exp_bound,
+                     "frac_of_exp_unit_bound": achieved / exp_bound},
         "cpu_baseline": cpu, "clocks": clk,
         "e2e": {"value": T / (e2e_ms / 1e3), "unit": "prompt tok/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": 2 * steps,
     }
-    print(json.dumps(line), flush=True)
-    return 0
 
 
 def e2e_cpu_baseline(model, n_req: int = 8, prompt_len: int = 32, gen: int = 16):
@@ -571,7 +628,7 @@ def e2e_cpu_baseline(model, n_req: int = 8, prompt_len: int = 32, gen: int = 16)
                       "numpy restatement of the reference engine and model with the same weights"}
 
 
-def run_e2e(args, rank: int, world: int, local_rank: int) -> int:
+def engine4_line(args, rank: int, world: int, local_rank: int):
     """Config 4: random-init TinyLlama-1.1B fp16 under continuous batching.  64 requests,
     prompt ids uniform in [3, 32000) with lengths U{32..512}, 128 greedy tokens each,
     four new requests before every engine step, max_batch_size 64, 4096 blocks of 16,
@@ -582,58 +639,78 @@ def run_e2e(args, rank: int, world: int, local_rank: int) -> int:
     from tinyvllm_b200.engine import LLMEngine, SamplingParams
     from tinyvllm_b200.model import Llama, tinyllama_config
 
-    torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    model = Llama(tinyllama_config("float16"), device=dev, seed=1234 + 4 + rank)
+    cfg = tinyllama_config("float16")
+    model = Llama(cfg, device=dev, seed=1234 + 4 + rank)
     rng = np.random.default_rng(1238 + rank)
     prompts = [rng.integers(3, 32000, size=int(rng.integers(32, 513))).tolist() for _ in range(64)]
     eng = LLMEngine(model, max_batch_size=64, num_blocks=4096, num_scheduler_steps=1, use_cuda_graphs=True)
+    steps = args.engine_steps
+    ctx_trace = []
 
-    def one_run():
+    def one_run(trace=False):
         i, made = 0, 0
         while i < len(prompts) or eng.has_unfinished():
             for _ in range(4):
                 if i < len(prompts):
                     eng.add_request(prompts[i], SamplingParams(max_tokens=128))
                     i += 1
+            if trace:
+                ctx_trace.append([s.get_len() for s in eng.scheduler.running.values()])
             made += sum(len(o.tokens) for o in eng.step())
         return made
 
-    for _ in range(max(args.warmup, 1)):
-        one_run()
+    one_run(trace=True)        # warm-up (graph captures) and the per-step context trace
     torch.cuda.synchronize(dev)
-    clocks = ClockSampler(world) if rank == 0 else None
+    clocks = ClockSampler(1) if rank == 0 else None
     if clocks:
         clocks.start()
         time.sleep(0.3)
     s0 = dict(eng.stats)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
-    made = sum(one_run() for _ in range(args.steps))
+    ev0.record()
+    made = sum(one_run() for _ in range(steps))
+    ev1.record()
     torch.cuda.synchronize(dev)
     dt = time.perf_counter() - t0
+    dev_s = ev0.elapsed_time(ev1) / 1e3
     clk = clocks.stop() if clocks else None
     if rank != 0:
-        return 0
-    dec_steps = eng.stats["decode_steps"] - s0["decode_steps"]
+        return None
+    dec_steps = (eng.stats["decode_steps"] - s0["decode_steps"]) // steps
+    # bytes one decode step must read: every weight once + the live K/V of the running batch
+    w_bytes = sum(p.numel() * p.element_size() for L in model.layers for p in (L.wqkv, L.wo, L.w13, L.w2)) \
+        + model.output.numel() * model.output.element_size()
+    tok_bytes = cfg.n_layers * cfg.n_kv_heads * cfg.head_dim * 2 * 2
+    kv_read = sum(min(c, 64 * 16) for step_ctx in ctx_trace for c in step_ctx) * tok_bytes
+    alg_bytes_run = w_bytes * len(ctx_trace) + kv_read
+    hbm, kind = _peaks()
+    achieved = alg_bytes_run / (dev_s / steps) / 1e9
     cpu = None if args.no_cpu_baseline else e2e_cpu_baseline(model)
-    line = {
+    del eng._graphs
+    return {
         "metric": "e2e decode tok/s (config 4: TinyLlama-1.1B fp16, 64 requests x 128 greedy tokens)",
-        "value": made / dt, "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 1),
-        "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "value": made / dev_s, "unit": "tok/s", "n_gpus": 1, "steps": steps, "warmup": 1,
+        "ms_per_step": dev_s * 1e3 / steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f16", "data": "synthetic (random-init weights N(0,0.02), random prompt ids)",
         "config": {"workload": "config4 e2e engine, staggered arrivals (4 per step), max_batch 64, 4096 blocks",
-                   "step": "one full run of the 64 requests", "generated_tokens_per_step": made // args.steps,
-                   "decode_steps_per_run": dec_steps // args.steps, "cuda_graphs": True},
+                   "step": "one full run of the 64 requests (prefills included)",
+                   "generated_tokens_per_step": made // steps, "engine_steps_per_run": len(ctx_trace),
+                   "decode_steps_per_run": dec_steps, "cuda_graphs": True},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_kind": kind,
+                     "note": "(weights once per engine step + live K/V each decode step reads) / run time; "
+                             "prefill FLOPs are not counted, so this is a lower bound on the HBM share"},
+        "wall_ms_per_step": dt * 1e3 / steps,
         "clocks": clk, "cpu_baseline": cpu,
         "gpu_launches": None,
-        "note": "wall clock with device syncs around whole engine runs (host scheduling included); the "
-                "engine mixes our kernels with cuBLAS GEMMs inside CUDA graphs, so no launch count is claimed",
+        "note": "device events around whole engine runs, host scheduling included (every engine step "
+                "synchronises); the engine mixes our kernels with cuBLAS GEMMs inside CUDA graphs",
     }
-    print(json.dumps(line), flush=True)
-    return 0
 
 
-def run_e2e8b(args, rank: int, world: int, local_rank: int) -> int:
+def engine5_line(args, rank: int, world: int, local_rank: int):
     """Config 5: random-init Llama-3-8B-shaped model in bf16; 512 sequences with
     contexts ~ U{512..8192} whose K/V is synthetic N(0,1) already in the pool,
     256 greedy tokens each, sharded by sequence over the ranks (least outstanding
@@ -641,7 +718,6 @@ def run_e2e8b(args, rank: int, world: int, local_rank: int) -> int:
     keeps resident as many of its sequences as its HBM holds (weights are
     replicated).  A step is one engine step (one decode iteration for every
     resident sequence on every rank); value = tokens produced by all ranks / s."""
-    import datetime
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -649,18 +725,11 @@ def run_e2e8b(args, rank: int, world: int, local_rank: int) -> int:
     from tinyvllm_b200.engine import LLMEngine, SamplingParams
     from tinyvllm_b200.model import Llama, llama3_8b_config
 
-    torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
-    else:
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        os.environ.setdefault("MASTER_PORT", "29533")
-        dist.init_process_group("nccl", device_id=dev, rank=0, world_size=1,
-                                timeout=datetime.timedelta(seconds=120))
     cfg = llama3_8b_config("bfloat16")
     model = Llama(cfg, device=dev, seed=1234 + 5)
     n_total, gen = 512, 256
+    steps, warmup = args.engine_steps_c5, 3
     rng = np.random.default_rng(1239)
     ctx = rng.integers(512, 8193, size=n_total)
     first = rng.integers(0, cfg.vocab_size, size=n_total)
@@ -673,7 +742,7 @@ def run_e2e8b(args, rank: int, world: int, local_rank: int) -> int:
         loads[r] += int(c) + gen
         if r == rank:
             mine.append(i)
-    steps_total = args.warmup + args.steps + 2
+    steps_total = warmup + steps + 2
     tok_bytes = cfg.n_layers * cfg.n_kv_heads * cfg.head_dim * 2 * 2
     free, _ = torch.cuda.mem_get_info(dev)
     budget = free - (8 << 30)                     # activations, graphs, workspaces
@@ -692,7 +761,7 @@ def run_e2e8b(args, rank: int, world: int, local_rank: int) -> int:
     sharded = ShardedEngine(eng, rank, world, dev)
     for i in range(n_total):
         sharded.add_request(prompts[i], SamplingParams(max_tokens=gen), prefilled_first_token=int(first[i]))
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         sharded.step()
     torch.cuda.synchronize(dev)
     dist.barrier(device_ids=[local_rank])
@@ -705,7 +774,7 @@ def run_e2e8b(args, rank: int, world: int, local_rank: int) -> int:
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
     ev0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         sharded.step()
     ev1.record()
     torch.cuda.synchronize(dev)
@@ -715,35 +784,86 @@ def run_e2e8b(args, rank: int, world: int, local_rank: int) -> int:
     made = sum(len(r.tokens) for r in sharded.requests.values()) - n0
     running = [s for s in eng.scheduler.running.values()]
     ctx_sum = sum(s.get_len() for s in running)
-    stats = torch.tensor([wall, ev0.elapsed_time(ev1) / 1e3, resident, ctx_sum], dtype=torch.float64, device=dev)
+    stats = torch.tensor([ev0.elapsed_time(ev1) / 1e3, wall, resident, ctx_sum], dtype=torch.float64, device=dev)
     allst = torch.empty(world * 4, dtype=torch.float64, device=dev)
     dist.all_gather_into_tensor(allst, stats)
     allst = allst.view(world, 4).cpu().numpy()
     del eng._graphs
+    if rank != 0:
+        return None
+    secs = float(allst[:, 0].max())
+    step_s = secs / steps
+    w_bytes = sum(p.numel() * p.element_size() for L in model.layers for p in
+                  (L.wqkv, L.wo, L.w13, L.w2)) + model.output.numel() * 2
+    kv_bytes = float(allst[0, 3]) * tok_bytes
+    hbm, kind = _peaks()
+    achieved = (w_bytes + kv_bytes) / step_s / 1e9
+    return {
+        "metric": "e2e decode tok/s (config 5: Llama-3-8B shape bf16, 512 seqs ctx U[512,8192], "
+                  "sequence-sharded)",
+        "value": made / secs, "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": warmup,
+        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (random-init weights, synthetic N(0,1) pre-filled K/V)",
+        "config": {"workload": "config5 sharded decode", "sequences": n_total,
+                   "resident_per_rank": [int(x) for x in allst[:, 2]],
+                   "ctx_sum_per_rank": [int(x) for x in allst[:, 3]],
+                   "parallelism": f"sequence-sharded x{world}, int32 token all-gather per step (NCCL)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "peak_kind": kind,
+                     "note": "rank 0: (weights + live K/V bytes per step) / step time"},
+        "timing": "device events around the timed engine steps, max over ranks (every step synchronises "
+                  "the host); wall clock max over ranks beside it",
+        "wall_ms_per_step": float(allst[:, 1].max()) / steps * 1e3,
+        "clocks": clk,
+    }
+
+
+def _free_cuda():
+    import gc
+    import torch
+    gc.collect()
+    torch.cuda.empty_cache()
+
+
+def run_ours(args, rank: int, world: int, local_rank: int) -> int:
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    _init_group(rank, world, dev)
+    line = decode_headline(args, rank, world, local_rank)
+    _free_cuda()
+    if not args.no_nested:
+        nested = {}
+        for key, fn in (("prefill", prefill_line), ("engine_config4", engine4_line),
+                        ("engine_config5", engine5_line)):
+            if key == "engine_config4" and world > 1:
+                continue                           # config 4 is a one-GPU workload
+            t0 = time.perf_counter()
+            res = fn(args, rank, world, local_rank)
+            _free_cuda()
+            dist.barrier(device_ids=[local_rank])
+            if rank == 0:
+                res["wall_s"] = time.perf_counter() - t0
+                nested[key] = res
+        if rank == 0:
+            line.update(nested)
     if rank == 0:
-        secs = float(allst[:, 0].max())
-        step_s = secs / args.steps
-        w_bytes = sum(p.numel() * p.element_size() for L in model.layers for p in
-                      (L.wqkv, L.wo, L.w13, L.w2)) + model.output.numel() * 2
-        kv_bytes = float(allst[0, 3]) * tok_bytes
-        hbm, kind = _peaks()
-        achieved = (w_bytes + kv_bytes) / step_s / 1e9
-        line = {
-            "metric": "e2e decode tok/s (config 5: Llama-3-8B shape bf16, 512 seqs ctx U[512,8192], "
-                      "sequence-sharded)",
-            "value": made / secs, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic (random-init weights, synthetic N(0,1) pre-filled K/V)",
-            "config": {"workload": "config5 sharded decode", "sequences": n_total,
-                       "resident_per_rank": [int(x) for x in allst[:, 2]],
-                       "ctx_sum_per_rank": [int(x) for x in allst[:, 3]],
-                       "parallelism": f"sequence-sharded x{world}, int32 token all-gather per step (NCCL)"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "peak_kind": kind,
-                         "note": "rank 0: (weights + live K/V bytes per step) / step time"},
-            "clocks": clk,
-        }
         print(json.dumps(line), flush=True)
+    dist.barrier(device_ids=[local_rank])
+    dist.destroy_process_group()
+    return 0
+
+
+def run_single(args, rank: int, world: int, local_rank: int, fn) -> int:
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    _init_group(rank, world, dev)
+    res = fn(args, rank, world, local_rank)
+    if rank == 0:
+        print(json.dumps(res), flush=True)
     dist.barrier(device_ids=[local_rank])
     dist.destroy_process_group()
     return 0
@@ -756,11 +876,16 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-nested", action="store_true",
+                    help="headline only: skip the nested prefill / engine configurations")
     ap.add_argument("--batch", type=int, default=256,
                     help="sequences per GPU (default 256 = config 3; smaller only for profiling captures)")
     ap.add_argument("--workload", choices=["decode", "prefill", "e2e", "e2e8b"], default="decode",
-                    help="decode = config 3 paged decode (the headline); prefill = config 2 flash prefill; "
+                    help="decode = config 3 headline (+ nested configurations); prefill = config 2 flash prefill; "
                          "e2e = config 4 TinyLlama engine; e2e8b = config 5 sharded Llama-3-8B-shape decode")
+    ap.add_argument("--prefill-steps", type=int, default=20)
+    ap.add_argument("--engine-steps", type=int, default=2, help="config-4 runs timed")
+    ap.add_argument("--engine-steps-c5", type=int, default=20, help="config-5 engine steps timed")
     ap.add_argument("--prefill-lens", default=None,
                     help="prefill workload: comma-separated prompt lengths (default: config 2's eight prompts)")
     ap.add_argument("--prefill-head-dim", type=int, choices=[64, 128], default=64)
@@ -775,11 +900,11 @@ def main() -> int:
     if args.impl == "reference":
         return run_reference(args, rank, world)
     if args.workload == "prefill":
-        return run_prefill(args, rank, world, local_rank)
+        return run_single(args, rank, world, local_rank, prefill_line)
     if args.workload == "e2e":
-        return run_e2e(args, rank, world, local_rank)
+        return run_single(args, rank, world, local_rank, engine4_line)
     if args.workload == "e2e8b":
-        return run_e2e8b(args, rank, world, local_rank)
+        return run_single(args, rank, world, local_rank, engine5_line)
     return run_ours(args, rank, world, local_rank)
 
 
