@@ -125,6 +125,9 @@ constexpr long kStaticTarget = 256;
 constexpr int kStaticMaxSplit = 1024;
 constexpr long kTargetUnits = kSlots * 4;
 constexpr int kMaxSplitTokens = 4096;
+// Block ids the producer keeps in registers per unit (a multiple of 32, at least
+// the largest stage's 64 / 8 = 8 blocks).
+constexpr int kBidWindow = 128;
 
 // One unit of decode work: one context split of one (sequence, KV head).
 // Tickets run over splits slowest, so every CTA sees a mix of sequences and
@@ -309,6 +312,11 @@ __global__ void __launch_bounds__(160, 2)
       const int tok_begin = live ? un.split * split_tokens : 0;
       const int ctx_end = live ? tok_begin + un.n_tok : 0;
       const int32_t* bt = live ? p.block_tables + (size_t)un.b * p.max_blocks : p.block_tables;
+      // The unit's block ids, kBidWindow at a time, one per lane and register, loaded
+      // once per window so that no stage waits on a table read before its copies.
+      const int blk_end = live ? (ctx_end + bs - 1) / bs : 0;  // one past the unit's last block
+      int win_base = -kBidWindow;                              // first block of the loaded window
+      int bid[kBidWindow / 32];
       for (int it = 0; it < n_stage; ++it, ++it_g) {
         const int s = it_g % C::kStages;
         const uint32_t ph = (it_g / C::kStages) & 1;
@@ -339,15 +347,32 @@ __global__ void __launch_bounds__(160, 2)
             ptx::bulk_load(qslot + s * q_bytes, qsrc, (uint32_t)q_bytes, &full_bar[s]);
           }
         }
+        const int first_blk = tok0 / bs;
+        if (first_blk + nblk > win_base + kBidWindow) {  // stage runs past the window: load the next one
+          win_base = first_blk;
+#pragma unroll
+          for (int r = 0; r < kBidWindow / 32; ++r) {
+            const int bi = win_base + r * 32 + lane;
+            bid[r] = bi < blk_end ? __ldg(bt + bi) : 0;
+          }
+        }
         __syncwarp();
         const uint32_t stage_off = s * C::kStageBytes;
         const int n_loads = nblk * C::kChunks * 2;
-        for (int i = lane; i < n_loads; i += 32) {
-          const int j = i / (C::kChunks * 2);
+        for (int i0 = 0; i0 < n_loads; i0 += 32) {  // warp-uniform trip count: every lane shuffles
+          const int i = i0 + lane;
+          const int j = min(i / (C::kChunks * 2), nblk - 1);
+          const int rel = first_blk + j - win_base;  // in [0, kBidWindow)
+          int blk = 0;
+#pragma unroll
+          for (int r = 0; r < kBidWindow / 32; ++r) {
+            const int v = __shfl_sync(0xffffffffu, bid[r], rel & 31);
+            blk = (rel >> 5) == r ? v : blk;
+          }
+          if (i >= n_loads) continue;
           const int rest = i % (C::kChunks * 2);
           const int kv = rest / C::kChunks;
           const int c = rest % C::kChunks;
-          const int blk = __ldg(bt + tok0 / bs + j);
           uint8_t* dst = base + stage_off + kv * C::kKVBytes + c * C::kChunkBytes + j * bs * RB;
           ptx::tma_load_4d(dst, kv ? &tm_v : &tm_k, &full_bar[s], c * RC, un.kvh, 0, blk);
         }
