@@ -122,9 +122,20 @@ int tvk_paged_decode_attention(const void* q, const void* k_cache, const void* v
  *              first int is set non-zero if a bounded wait expired.
  * fp16/bf16 with head_dim 64 or 128 run on tcgen05 (TMEM accumulators, TMA
  * loads, persistent CTAs over a heaviest-first tile schedule built on the
- * device); fp32 and head_dim 32 use a CUDA-core kernel.  Softmax is fp32.
+ * device; see tvk_prefill_select_kernel); fp32 and head_dim 32 use a CUDA-core
+ * kernel.  Softmax is fp32.
  */
 size_t tvk_flash_prefill_workspace_size(int n_seqs, int total_tokens);
+
+/*
+ * Selects the tensor-core prefill kernel for later tvk_flash_prefill_attention
+ * calls on the calling thread: 0 (default) = automatic -- the paired-head kernel
+ * (two query heads that share a KV head per CTA item, one CTA per SM) whenever
+ * n_heads / n_kv_heads is even, else the one-head kernel; 1 = always the
+ * one-head kernel.  Both compute the same function; this exists so tests and
+ * timings can run either.  No counterpart in the reference.
+ */
+int tvk_prefill_select_kernel(int choice);
 int tvk_flash_prefill_attention(const void* q, const void* k, const void* v, void* out,
                                 const int32_t* cu_seqlens, int n_seqs, int max_seqlen, int total_tokens,
                                 int n_heads, int n_kv_heads, int head_dim, int causal, int dtype,

@@ -55,6 +55,17 @@ def _oracle(q, k, v, causal=True):
 DTYPES = [torch.float32, torch.float16, torch.bfloat16]
 
 
+@pytest.fixture(params=[0, 1], ids=["auto", "one_head"])
+def kernel(request, cuda):
+    """Runs the test with the automatic kernel choice (the paired-head kernel where
+    the query heads per KV head are even) and again with the one-head kernel."""
+    from tinyvllm_b200 import _lib
+    lib = _lib.lib()
+    assert lib.tvk_prefill_select_kernel(request.param) == 0
+    yield request.param
+    assert lib.tvk_prefill_select_kernel(0) == 0
+
+
 # tests/test_flash_attention.py shapes
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("L", [1, 2, 7, 8, 15, 16, 31, 32, 63, 64, 128])
@@ -68,7 +79,7 @@ def test_lengths_and_head_dims(cuda, dtype, L, D):
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("L,nh,nkv,D", [(16, 8, 4, 32), (16, 32, 8, 64), (16, 32, 4, 64), (32, 32, 8, 64),
                                         (64, 32, 8, 64), (256, 32, 8, 64), (200, 32, 4, 128), (1, 8, 8, 64)])
-def test_gqa(cuda, dtype, L, nh, nkv, D):
+def test_gqa(cuda, kernel, dtype, L, nh, nkv, D):
     g = torch.Generator(device=cuda).manual_seed(L + nh + nkv + D)
     q = _rand((L, nh, D), dtype, g, cuda)
     k = _rand((L, nkv, D), dtype, g, cuda)
@@ -117,7 +128,7 @@ def _config2_inputs(dev, dtype=torch.float16, lens=(1, 15, 16, 17, 128, 500, 102
 
 
 @pytest.mark.parametrize("dtype,D,nkv", [(torch.float16, 64, 4), (torch.bfloat16, 128, 8), (torch.float32, 64, 4)])
-def test_config2_ragged_batch_with_paged_write(cuda, dtype, D, nkv):
+def test_config2_ragged_batch_with_paged_write(cuda, kernel, dtype, D, nkv):
     """Config 2: 8 ragged prompts in one call; attention vs oracle per prompt and the
     paged pool bit-exact against the reference slot mapping (LIFO allocation)."""
     from tinyvllm_b200.attention import flash_prefill_attention_varlen
@@ -142,7 +153,7 @@ def test_config2_ragged_batch_with_paged_write(cuda, dtype, D, nkv):
         _check(out[a:b], _oracle(q[a:b], k[a:b], v[a:b]), dtype)
 
 
-def test_paged_write_matches_chunked_reference_write(cuda):
+def test_paged_write_matches_chunked_reference_write(cuda, kernel):
     """The fused write equals the reference's block-chunked write_kv sequence
     (llama.py:188-209) replayed by the oracle on the same BlockManager state."""
     from tinyvllm_b200.attention import flash_prefill_attention_varlen
@@ -168,7 +179,7 @@ def test_paged_write_matches_chunked_reference_write(cuda):
     assert np.array_equal(vc.cpu().numpy(), cache.v_cache[0])
 
 
-def test_negative_slots_are_skipped(cuda):
+def test_negative_slots_are_skipped(cuda, kernel):
     from tinyvllm_b200.attention import flash_prefill_attention_varlen
     q, k, v, cu, lens = _config2_inputs(cuda, torch.float16, lens=[20])
     slots = torch.arange(20, dtype=torch.int64, device=cuda)
@@ -184,7 +195,7 @@ def test_negative_slots_are_skipped(cuda):
     assert torch.count_nonzero(flat[3]) == 0 and torch.count_nonzero(flat[7]) == 0
 
 
-def test_repeat_calls_are_deterministic(cuda):
+def test_repeat_calls_are_deterministic(cuda, kernel):
     from tinyvllm_b200.attention import flash_prefill_attention_varlen
     q, k, v, cu, lens = _config2_inputs(cuda, torch.float16)
     a = flash_prefill_attention_varlen(q, k, v, cu, max(lens)).clone()
@@ -194,7 +205,7 @@ def test_repeat_calls_are_deterministic(cuda):
 
 
 @pytest.mark.parametrize("n", [33, 70])
-def test_many_prompts_take_the_device_schedule(cuda, n):
+def test_many_prompts_take_the_device_schedule(cuda, kernel, n):
     """More than 32 prompts: the work list is built by the schedule kernel rather
     than by the producer warps; alternating with a small batch on the same
     workspace checks that every call returns the item counters to zero."""
@@ -216,3 +227,56 @@ def test_many_prompts_take_the_device_schedule(cuda, n):
             _check(out_s[a:b], _oracle(sq[a:b], sk[a:b], sv[a:b]), torch.float16)
     from tinyvllm_b200.attention import workspace_status
     assert workspace_status(kind="prefill") == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("L,nh,nkv,D", [(300, 32, 4, 64), (129, 8, 2, 64), (260, 32, 8, 128), (1, 16, 4, 64)])
+def test_non_causal_gqa(cuda, kernel, dtype, L, nh, nkv, D):
+    g = torch.Generator(device=cuda).manual_seed(L * 3 + nh + D)
+    q = _rand((L, nh, D), dtype, g, cuda)
+    k = _rand((L, nkv, D), dtype, g, cuda)
+    v = _rand((L, nkv, D), dtype, g, cuda)
+    _check(_flash(q, k, v, causal=False), _oracle(q, k, v, causal=False), dtype)
+
+
+@pytest.mark.parametrize("dtype,D,nkv", [(torch.float16, 64, 4), (torch.bfloat16, 128, 8)])
+def test_running_max_jumps(cuda, kernel, dtype, D, nkv):
+    """Keys grow along the prompt, so the running row max rises by more than 2^8
+    several times: the lazy O rescale (skipped while the max grows less) runs."""
+    g = torch.Generator(device=cuda).manual_seed(77 + D)
+    L = 700
+    ramp = (0.25 + torch.arange(L, device=cuda, dtype=torch.float32) / 48.0)[:, None, None]
+    q = _rand((L, 32, D), dtype, g, cuda)
+    k = (torch.randn(L, nkv, D, generator=g, device=cuda) * ramp).to(dtype)
+    v = _rand((L, nkv, D), dtype, g, cuda)
+    _check(_flash(q, k, v), _oracle(q, k, v), dtype)
+
+
+@pytest.mark.parametrize("dtype,D,nkv", [(torch.float16, 64, 4), (torch.bfloat16, 128, 8)])
+def test_long_prompts(cuda, kernel, dtype, D, nkv):
+    """Two 2,500-token prompts: items of up to 20 key tiles, the K/V ring and both Q
+    buffers wrap many times inside one CTA."""
+    from tinyvllm_b200.attention import flash_prefill_attention_varlen
+    q, k, v, cu, lens = _config2_inputs(cuda, dtype, lens=(2500, 1900), D=D, nkv=nkv)
+    out = flash_prefill_attention_varlen(q, k, v, cu, max(lens))
+    torch.cuda.synchronize()
+    for i in range(2):
+        a, b = int(cu[i]), int(cu[i + 1])
+        _check(out[a:b], _oracle(q[a:b], k[a:b], v[a:b]), dtype)
+
+
+def test_both_kernels_agree_on_config2(cuda):
+    """The paired-head and one-head kernels compute the same function: on config 2
+    they agree to within one output rounding."""
+    from tinyvllm_b200 import _lib
+    from tinyvllm_b200.attention import flash_prefill_attention_varlen
+    lib = _lib.lib()
+    q, k, v, cu, lens = _config2_inputs(cuda, torch.float16)
+    outs = []
+    for choice in (0, 1):
+        assert lib.tvk_prefill_select_kernel(choice) == 0
+        outs.append(flash_prefill_attention_varlen(q, k, v, cu, max(lens)).clone())
+    assert lib.tvk_prefill_select_kernel(0) == 0
+    torch.cuda.synchronize()
+    diff = (outs[0].float() - outs[1].float()).abs().max().item()
+    assert diff <= 4e-3, diff

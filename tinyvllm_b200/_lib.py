@@ -45,6 +45,7 @@ SIGNATURES = {
     "tvk_embedding": (_c_int, [_c_void] * 3 + [_c_int] * 4 + [_c_void, _c_void]),
     "tvk_argmax": (_c_int, [_c_void] * 2 + [_c_int, _c_int, _c_int64, _c_int, _c_void]),
     "tvk_flash_prefill_workspace_size": (_c_size, [_c_int] * 2),
+    "tvk_prefill_select_kernel": (_c_int, [_c_int]),
     "tvk_flash_prefill_attention": (
         _c_int,
         [_c_void] * 5 + [_c_int] * 8 + [_c_void] * 3 + [_c_int] * 2 + [_c_void, _c_size, _c_void],

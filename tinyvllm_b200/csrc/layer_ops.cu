@@ -334,7 +334,29 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const T* __restr
   float bv = -INFINITY;
   int bi = 0x7fffffff;
   const int nvec = vec ? vocab / N : 0;  // 16-byte loads only when every row is 16-byte aligned
-  for (int i = threadIdx.x; i < nvec; i += blockDim.x) {
+  // Four independent 16-byte loads in flight per thread (the compare order does not
+  // matter: ties go to the lower index whatever the order).
+  constexpr int U = 4;
+  int i = threadIdx.x;
+  for (; i + (U - 1) * (int)blockDim.x < nvec; i += U * blockDim.x) {
+    uint4 u[U];
+#pragma unroll
+    for (int k = 0; k < U; ++k) u[k] = __ldg(reinterpret_cast<const uint4*>(row + (size_t)(i + k * blockDim.x) * N));
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      const T* h = reinterpret_cast<const T*>(&u[k]);
+      const int i0 = (i + k * blockDim.x) * N;
+#pragma unroll
+      for (int e = 0; e < N; ++e) {
+        const float f = DT<T>::to_f(h[e]);
+        if (better(f, i0 + e, bv, bi)) {
+          bv = f;
+          bi = i0 + e;
+        }
+      }
+    }
+  }
+  for (; i < nvec; i += blockDim.x) {
     float f[N];
     load_vec<T>(row + (size_t)i * N, f);
 #pragma unroll

@@ -581,6 +581,521 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
 }
 
 // -----------------------------------------------------------------------------
+// Paired-head tcgen05 kernel (fp16/bf16, head_dim 64 or 128, an even number of
+// query heads per KV head).  One CTA per SM walks the heaviest-first item list;
+// an item is one 128-row query tile of a PAIR of query heads (h, h+1) that read
+// the same KV head, so every K/V tile is loaded once for both.  Keys come in
+// tiles of 128.  12 warps in three warpgroups:
+//   warp 0      TMA producer: both heads' Q tiles once per item, then the K/V
+//               ring; copies the diagonal tile's landed K/V rows into their
+//               paged slots when the pair holds the KV group's first head.
+//   warp 1      TMEM owner; issues S_t = Q_t.K^T for both heads t = 0, 1
+//               (M=128, N=128) from one thread.
+//   warps 2, 3  issue O_t += P_t.V for head 0 and head 1 (A = P_t from TMEM,
+//               N = head_dim).  One thread issues an MMA about every 130
+//               cycles whatever its size, so the three issuers keep the tensor
+//               pipe fed where one could not (a key tile is 24 MMAs).
+//   warps 4-7   softmax of head h, warps 8-11 softmax of head h+1: one query
+//               row per thread, 128 scores per key tile in registers, online
+//               softmax in the log2 domain with a lazy O rescale, P packed to
+//               16-bit pairs into TMEM, row sums in fp32 registers; at the end
+//               of an item the same threads normalise O and store the rows.
+// TMEM columns, head_dim 64:  S0 0-127, S1 128-255, P0 256-319, P1 320-383,
+//                              O0 384-447, O1 448-511 (P apart from S, so the
+//                              next S never waits for the previous P.V).
+//              head_dim 128: S0 0-127 (P0 over its first 64), S1 128-255 (P1),
+//                              O0 256-383, O1 384-511.
+// -----------------------------------------------------------------------------
+template <int D>
+struct PairCfg {
+  static constexpr int kKB = D / 64;                    // 64-element (128 B) column blocks
+  static constexpr int kRows = 128;                     // query rows per tile = keys per K/V tile
+  static constexpr int kBlockBytes = kRows * 128;       // one column block of a 128-row tile
+  static constexpr int kTileBytes = kRows * D * 2;      // one 128-row tile (Q of one head, K or V)
+  static constexpr int kQBufs = D == 64 ? 2 : 1;        // Q buffers (items in flight), two heads each
+  static constexpr int kStages = D == 64 ? 4 : 2;       // K/V ring depth
+  static constexpr int kQOff = 0;
+  static constexpr int kKOff = kQOff + kQBufs * 2 * kTileBytes;
+  static constexpr int kVOff = kKOff + kStages * kTileBytes;
+  static constexpr int kBarOff = kVOff + kStages * kTileBytes;
+  static constexpr int kItemSlots = 4;
+  // q_full[QB], q_empty[QB], k_full[S], v_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2],
+  // pv_done[2], o_empty[2], final[3], item_full[4], item_empty[4]
+  static constexpr int kNumBars = 2 * kQBufs + 3 * kStages + 10 + 3 + 2 * kItemSlots;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+  static constexpr int kUsed = kMiscOff + 16 + 32 * kItemSlots;
+  static constexpr int kSmemBytes = kUsed + 1024;
+  static_assert(kSmemBytes <= 232448, "shared memory per CTA");
+  static constexpr bool kPAlias = D == 128;             // P written over the first half of its S
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr int kThreads = 384;
+  // register split (setmaxnreg): warpgroup 0 drops to kRegsLow, the two softmax
+  // warpgroups rise to kRegsHigh; the launch must provide 384 x kRegsLaunchMin.
+  static constexpr int kRegsLow = 56, kRegsHigh = 224;
+  static constexpr int kRegsLaunchMin = (128 * kRegsLow + 256 * kRegsHigh + kThreads - 1) / kThreads;
+};
+
+__device__ __forceinline__ uint32_t pcol(int D, int t) {
+  return D == 128 ? (t ? 128u : 0u) : (t ? 320u : 256u);
+}
+__device__ __forceinline__ uint32_t ocol(int D, int t) {
+  return D == 128 ? (t ? 384u : 256u) : (t ? 448u : 384u);
+}
+
+// One unit of work of the paired kernel: a 128-row query tile of heads (h0, h0+1).
+struct PairItem {
+  int seq, mtile, h0, s0, L;
+};
+
+__device__ __forceinline__ PairItem pair_item_of(const PrefillParams& p, int w) {
+  const int n_pairs = p.n_heads >> 1;
+  const int e = __ldcg(p.sched + w / n_pairs);
+  const int seq = e >> 16, m = e & 0xFFFF;
+  if (seq < 0 || seq >= p.n_seqs || m >= p.n_mtiles) return PairItem{-1, 0, 0, 0, 0};
+  const int s0 = __ldcg(p.cu_seqlens + seq);
+  const int L = __ldcg(p.cu_seqlens + seq + 1) - s0;
+  if (s0 < 0 || L <= m * 128 || s0 + L > p.total_tokens) return PairItem{-1, 0, 0, 0, 0};
+  return PairItem{seq, m, 2 * (w % n_pairs), s0, L};
+}
+
+// 128-key tiles an item visits: up to and including the diagonal when causal.
+__device__ __forceinline__ int pair_kv_tiles(const PrefillParams& p, const PairItem& it) {
+  const int all = (it.L + 127) / 128;
+  return p.causal ? min(it.mtile + 1, all) : all;
+}
+
+__device__ __forceinline__ void add2(float& a0, float& a1, float b0, float b1) {
+  uint64_t A, B, Dd;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(A) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(B) : "f"(b0), "f"(b1));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(Dd) : "l"(A), "l"(B));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(Dd));
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(384, 1)
+    flash_prefill_pair_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tm_q,
+                              const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
+  using C = PairCfg<D>;
+  constexpr int S = C::kStages;
+  constexpr int QB = C::kQBufs;
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_u32 = ptx::smem_u32(smem_raw);
+  const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
+  if (base_u32 + C::kUsed > raw_u32 + C::kSmemBytes) {  // cannot happen with a >=16 B aligned base
+    if (threadIdx.x == 0) report(p.status);
+    return;
+  }
+  uint8_t* base = smem_raw + (base_u32 - raw_u32);
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(base + C::kBarOff);
+  uint64_t* q_empty = q_full + QB;
+  uint64_t* k_full = q_empty + QB;
+  uint64_t* v_full = k_full + S;
+  uint64_t* kv_empty = v_full + S;
+  uint64_t* s_full = kv_empty + S;  // [2] per head
+  uint64_t* s_free = s_full + 2;
+  uint64_t* p_full = s_free + 2;
+  uint64_t* pv_done = p_full + 2;
+  uint64_t* o_empty = pv_done + 2;
+  uint64_t* final_bar = o_empty + 2;  // [3] one per MMA-issuing warp
+  uint64_t* item_full = final_bar + 3;
+  uint64_t* item_empty = item_full + C::kItemSlots;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + C::kMiscOff);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(base + C::kMiscOff + 4);
+  volatile int* item_ring = reinterpret_cast<volatile int*>(base + C::kMiscOff + 16);  // [slot][8]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp == 1) {
+    umma::tmem_alloc(tmem_slot, C::kTmemCols);
+    umma::tmem_relinquish();
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < QB; ++i) {
+      ptx::mbar_init(&q_full[i], 1);
+      ptx::mbar_init(&q_empty[i], 1);
+    }
+    for (int s = 0; s < S; ++s) {
+      ptx::mbar_init(&k_full[s], 1);
+      ptx::mbar_init(&v_full[s], 1);
+      ptx::mbar_init(&kv_empty[s], 3);  // the S issuer and both P.V issuers
+    }
+    for (int t = 0; t < 2; ++t) {
+      ptx::mbar_init(&s_full[t], 1);
+      ptx::mbar_init(&s_free[t], 4);
+      ptx::mbar_init(&p_full[t], 4);
+      ptx::mbar_init(&pv_done[t], 1);
+      ptx::mbar_init(&o_empty[t], 4);
+    }
+    for (int i = 0; i < 3; ++i) ptx::mbar_init(&final_bar[i], 1);
+    for (int i = 0; i < C::kItemSlots; ++i) {
+      ptx::mbar_init(&item_full[i], 1);
+      ptx::mbar_init(&item_empty[i], 11);  // the three MMA issuers and the eight softmax warps
+    }
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int n_items = min(__ldcg(p.sched_count), p.sched_cap) * (p.n_heads >> 1);
+  uint32_t n_seen = 0;
+  auto take_item = [&](PairItem& it, bool arrive) -> int {  // 1: item, 0: end of list, -1: gave up
+    const int slot = n_seen % C::kItemSlots;
+    if (!wait_or_abort(&item_full[slot], (n_seen / C::kItemSlots) & 1, abort_flag, p.wait_ns)) return -1;
+    volatile int* e = item_ring + slot * 8;
+    it = PairItem{e[0], e[1], e[2], e[3], e[4]};
+    if (arrive) ptx::mbar_arrive(&item_empty[slot]);
+    ++n_seen;
+    return it.seq < 0 ? 0 : 1;
+  };
+
+  // Each warpgroup sets its register share at the top of its own branch (code
+  // after a join is held to the smaller share).
+  if (warp < 4) {
+   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::kRegsLow));
+   if (warp == 0) {
+    // =========================== TMA producer ===============================
+    uint32_t kv_it = 0, q_it = 0, n_claim = 0;
+    bool ok = true;
+    if (lane == 0) {
+      ptx::prefetch_tmap(&tm_q);
+      ptx::prefetch_tmap(&tm_k);
+      ptx::prefetch_tmap(&tm_v);
+    }
+    const long long n_slots = (long long)p.num_blocks * p.block_size;
+    PairItem it{};
+    while (ok) {
+      const int slot = n_claim % C::kItemSlots;
+      int w = 0;
+      if (lane == 0) w = (int)atomicAdd(p.ticket, 1);
+      w = __shfl_sync(0xffffffffu, w, 0);
+      if (w >= n_items) w = -1;
+      if (w >= 0) {
+        it = pair_item_of(p, w);
+        if (it.seq < 0) {  // a corrupt schedule entry: stop here and say so
+          report(p.status);
+          w = -1;
+        }
+      }
+      ok = __all_sync(0xffffffffu,
+                      wait_or_abort(&item_empty[slot], ((n_claim / C::kItemSlots) & 1) ^ 1, abort_flag, p.wait_ns));
+      if (!ok) break;
+      if (lane == 0) {
+        volatile int* e = item_ring + slot * 8;
+        e[0] = w < 0 ? -1 : it.seq;
+        e[1] = it.mtile;
+        e[2] = it.h0;
+        e[3] = it.s0;
+        e[4] = it.L;
+        ptx::mbar_arrive(&item_full[slot]);
+      }
+      ++n_claim;
+      if (w < 0) break;
+      if (p.drop_loads) break;  // test hook: the item's Q and K/V never arrive
+      const int n_kv = pair_kv_tiles(p, it);
+      const int kvh = it.h0 / p.group;
+      const int qb = q_it % QB;
+      ok = __all_sync(0xffffffffu, wait_or_abort(&q_empty[qb], ((q_it / QB) & 1) ^ 1, abort_flag, p.wait_ns));
+      if (!ok) break;
+      if (lane == 0) {
+        ptx::mbar_arrive_expect_tx(&q_full[qb], 2 * C::kTileBytes);
+        for (int t = 0; t < 2; ++t)
+          for (int kb = 0; kb < C::kKB; ++kb)
+            tma_load_3d(base + C::kQOff + (qb * 2 + t) * C::kTileBytes + kb * C::kBlockBytes, &tm_q, &q_full[qb],
+                        kb * 64, it.h0 + t, it.s0 + it.mtile * 128);
+      }
+      ++q_it;
+      const bool write_kv = p.slot_mapping != nullptr && (it.h0 % p.group) == 0;
+      for (int j = 0; j < n_kv; ++j, ++kv_it) {
+        const int st = kv_it % S;
+        const uint32_t ph = (kv_it / S) & 1;
+        ok = __all_sync(0xffffffffu, wait_or_abort(&kv_empty[st], ph ^ 1, abort_flag, p.wait_ns));
+        if (!ok) break;
+        uint8_t* ks = base + C::kKOff + st * C::kTileBytes;
+        uint8_t* vs = base + C::kVOff + st * C::kTileBytes;
+        if (lane == 0) {
+          ptx::mbar_arrive_expect_tx(&k_full[st], C::kTileBytes);
+          for (int kb = 0; kb < C::kKB; ++kb)
+            tma_load_3d(ks + kb * C::kBlockBytes, &tm_k, &k_full[st], kb * 64, kvh, it.s0 + j * 128);
+          ptx::mbar_arrive_expect_tx(&v_full[st], C::kTileBytes);
+          for (int kb = 0; kb < C::kKB; ++kb)
+            tma_load_3d(vs + kb * C::kBlockBytes, &tm_v, &v_full[st], kb * 64, kvh, it.s0 + j * 128);
+        }
+        if (write_kv && j == it.mtile) {
+          // The diagonal tile holds exactly this query tile's own tokens: copy the
+          // landed rows into their paged slots (slot = block * block_size + offset).
+          ok = __all_sync(0xffffffffu, wait_or_abort(&k_full[st], ph, abort_flag, p.wait_ns) &&
+                                           wait_or_abort(&v_full[st], ph, abort_flag, p.wait_ns));
+          if (!ok) break;
+          const int tok0 = it.s0 + j * 128, rows = min(128, it.L - j * 128);
+          T* kc = reinterpret_cast<T*>(p.k_cache);
+          T* vc = reinterpret_cast<T*>(p.v_cache);
+          long long sl[4];  // slots of rows lane, lane + 32, lane + 64, lane + 96
+#pragma unroll
+          for (int q = 0; q < 4; ++q) sl[q] = lane + 32 * q < rows ? __ldcg(p.slot_mapping + tok0 + lane + 32 * q) : -1;
+          for (int i0 = 0; i0 < rows * (D / 8); i0 += 32) {
+            const int i = i0 + lane;
+            const int r = min(i / (D / 8), 127), c8 = i % (D / 8);
+            long long slot = -1;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const long long v = __shfl_sync(0xffffffffu, sl[q], r & 31);
+              slot = (r >> 5) == q ? v : slot;
+            }
+            if (i >= rows * (D / 8) || slot < 0 || slot >= n_slots) continue;
+            const uint32_t off = (c8 / 8) * C::kBlockBytes + r * 128 + ((((c8 & 7) ^ (r & 7))) << 4);
+            const size_t dst = ((size_t)slot * p.n_kv_heads + kvh) * D + c8 * 8;
+            *reinterpret_cast<uint4*>(kc + dst) = *reinterpret_cast<const uint4*>(ks + off);
+            *reinterpret_cast<uint4*>(vc + dst) = *reinterpret_cast<const uint4*>(vs + off);
+          }
+        }
+      }
+    }
+    if (!ok) report(p.status);
+    // Do not leave with copies in flight: the last issued loads must have landed.
+    if (lane == 0) {
+      for (uint32_t j = kv_it >= (uint32_t)S ? kv_it - S : 0; j < kv_it; ++j) {
+        ptx::mbar_wait(&k_full[j % S], (j / S) & 1, 100000000ull);
+        ptx::mbar_wait(&v_full[j % S], (j / S) & 1, 100000000ull);
+      }
+      for (uint32_t j = q_it >= (uint32_t)QB ? q_it - QB : 0; j < q_it; ++j)
+        ptx::mbar_wait(&q_full[j % QB], (j / QB) & 1, 100000000ull);
+    }
+  } else if (warp == 1) {
+    // ======================= S issuer (both heads) ==========================
+    if (lane == 0) {
+      const uint32_t idesc_s = umma::idesc_f16(128, 128, kBf16, false);
+      uint32_t g = 0, q_it = 0;  // g: K/V tiles of this CTA
+      bool ok = true;
+      PairItem it;
+      while (ok) {
+        const int got = take_item(it, true);
+        if (got <= 0) {
+          ok = got == 0;
+          break;
+        }
+        const int n_kv = pair_kv_tiles(p, it);
+        const int qb = q_it % QB;
+        ok = wait_or_abort(&q_full[qb], (q_it / QB) & 1, abort_flag, p.wait_ns);
+        for (int j = 0; ok && j < n_kv; ++j, ++g) {
+          ok = wait_or_abort(&k_full[g % S], (g / S) & 1, abort_flag, p.wait_ns);
+          const uint32_t k_addr = base_u32 + C::kKOff + (g % S) * C::kTileBytes;
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (C::kPAlias) {
+              // P_t lives over S_t: S_t(g) waits for P_t(g-1).V to complete (which
+              // also means softmax t has read S_t(g-1)).
+              if (g > 0) ok = wait_or_abort(&pv_done[t], (g - 1) & 1, abort_flag, p.wait_ns);
+            } else {
+              ok = wait_or_abort(&s_free[t], (g & 1) ^ 1, abort_flag, p.wait_ns);  // S_t(g-1) was read
+            }
+            if (!ok) break;
+            umma::fence_after_sync();
+            const uint32_t q_addr = base_u32 + C::kQOff + (qb * 2 + t) * C::kTileBytes;
+#pragma unroll
+            for (int ks = 0; ks < D / 16; ++ks) {
+              const uint64_t ad = umma::smem_desc_sw128(q_addr + (ks >> 2) * C::kBlockBytes + (ks & 3) * 32, 16, 1024);
+              const uint64_t bd = umma::smem_desc_sw128(k_addr + (ks >> 2) * C::kBlockBytes + (ks & 3) * 32, 16, 1024);
+              umma::mma_f16_ss(tmem + (t ? 128u : 0u), ad, bd, idesc_s, ks > 0 ? 1u : 0u);
+            }
+            umma::commit(&s_full[t]);
+          }
+          if (!ok) break;
+          umma::commit(&kv_empty[g % S]);                 // K(g) consumed
+          if (j == n_kv - 1) umma::commit(&q_empty[qb]);  // Q is free once the item's S MMAs are done
+        }
+        ++q_it;
+      }
+      if (!ok) report(p.status);
+      // Drain: every MMA issued by this thread completes before TMEM is released.
+      umma::commit(&final_bar[0]);
+      ptx::mbar_wait(&final_bar[0], 0, 100000000ull);
+    }
+    __syncwarp();
+  } else if (warp == 2 || warp == 3) {
+    // ===================== P.V issuer of head t = warp - 2 ===================
+    if (lane == 0) {
+      const int t = warp - 2;
+      const uint32_t idesc_o = umma::idesc_f16(128, D, kBf16, true);
+      uint32_t g = 0, item_it = 0;
+      bool ok = true;
+      PairItem it;
+      while (ok) {
+        const int got = take_item(it, true);
+        if (got <= 0) {
+          ok = got == 0;
+          break;
+        }
+        const int n_kv = pair_kv_tiles(p, it);
+        for (int j = 0; ok && j < n_kv; ++j, ++g) {
+          ok = wait_or_abort(&v_full[g % S], (g / S) & 1, abort_flag, p.wait_ns) &&
+               wait_or_abort(&p_full[t], g & 1, abort_flag, p.wait_ns);
+          // the item's first P.V overwrites O_t: the previous item's O_t must have been read
+          if (ok && j == 0) ok = wait_or_abort(&o_empty[t], (item_it & 1) ^ 1, abort_flag, p.wait_ns);
+          if (!ok) break;
+          umma::fence_after_sync();
+          const uint32_t v_addr = base_u32 + C::kVOff + (g % S) * C::kTileBytes;
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {  // 16 keys per MMA: 8 TMEM columns of P
+            const uint64_t bd = umma::smem_desc_sw128(v_addr + ks * 2048, C::kBlockBytes, 1024);
+            umma::mma_f16_ts(tmem + ocol(D, t), tmem + pcol(D, t) + ks * 8, bd, idesc_o, (j == 0 && ks == 0) ? 0u : 1u);
+          }
+          umma::commit(&pv_done[t]);
+          umma::commit(&kv_empty[g % S]);  // V(g) consumed by this head
+        }
+        ++item_it;
+      }
+      if (!ok) report(p.status);
+      umma::commit(&final_bar[warp - 1]);
+      ptx::mbar_wait(&final_bar[warp - 1], 0, 100000000ull);
+    }
+    __syncwarp();
+   }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(C::kRegsHigh));
+    // =========================== softmax warps ==============================
+    const int t = (warp - 4) >> 2;     // head of the pair
+    const int quarter = warp & 3;      // TMEM lane quarter this warp may access
+    const int r = quarter * 32 + lane; // query row of the tile
+    const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+    const uint32_t s_col = t ? 128u : 0u, p_col = pcol(D, t), o_col = ocol(D, t);
+    const float sl2 = p.scale_log2;
+    uint32_t g = 0;  // K/V tiles seen (S, P and P.V phases follow it)
+    bool ok = true;
+    PairItem it;
+    while (ok) {
+      int got = take_item(it, false);
+      ok = __all_sync(0xffffffffu, got >= 0);
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&item_empty[(n_seen - 1) % C::kItemSlots]);
+      if (got == 0) break;
+      const int n_kv = pair_kv_tiles(p, it);
+      const int q_pos = it.mtile * 128 + r;
+      const int lim = p.causal ? min(q_pos + 1, it.L) : it.L;  // keys [0, lim) are visible
+      float m = -INFINITY;  // running max (log2 domain) that P and O are scaled by
+      float l0 = 0.f, l1 = 0.f;
+      for (int j = 0; j < n_kv; ++j, ++g) {
+        ok = __all_sync(0xffffffffu, wait_or_abort(&s_full[t], g & 1, abort_flag, p.wait_ns));
+        if (!ok) break;
+        umma::fence_after_sync();
+        float s[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          umma::ld_32x32b_x32(t_lane + s_col + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
+        umma::ld_wait();
+        if (!C::kPAlias) {  // S_t is free for the next tile's scores
+          umma::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&s_free[t]);
+        }
+        const int lim_rel = lim - j * 128;  // keys [0, lim_rel) of this tile are visible
+        if (__any_sync(0xffffffffu, lim_rel < 128)) {
+#pragma unroll
+          for (int x = 0; x < 128; ++x) s[x] = x < lim_rel ? s[x] : -INFINITY;
+        }
+        float mp[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          mp[i] = max3f(s[i], s[8 + i], s[16 + i]);
+#pragma unroll
+          for (int k = 24; k < 128; k += 16) mp[i] = max3f(mp[i], s[k + i], s[k + 8 + i]);
+        }
+        const float mx = max3f(max3f(mp[0], mp[1], mp[2]), max3f(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
+        float m_cand = fmaxf(m, mx * sl2);
+        if (m_cand == -INFINITY) m_cand = 0.f;  // no visible key (a row past the prompt's end)
+        // P_t's columns (and, when P lives over S, nothing else) are rewritten below:
+        // the previous tile's P_t.V must have completed.
+        if (g > 0) {
+          ok = __all_sync(0xffffffffu, wait_or_abort(&pv_done[t], (g - 1) & 1, abort_flag, p.wait_ns));
+          if (!ok) break;
+          umma::fence_after_sync();
+        }
+        // Lazy rescale: the stale max is kept unless the new one is 2^8 larger; O_t
+        // itself is rescaled after P is stored (the scores are dead by then), still
+        // before P_t.V is released to add to it.
+        float corr = 1.f;
+        const bool rescale = j > 0 && __any_sync(0xffffffffu, m_cand > m + 8.f);
+        if (j == 0 || rescale) {
+          corr = j == 0 ? 1.f : ex2(m - m_cand);
+          l0 *= corr;
+          l1 *= corr;
+          m = m_cand;
+        }
+        // P = 2^(s*scale - m), packed to 16-bit pairs: the A operand of P.V
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int x = 0; x < 32; ++x) {
+            float x0, x1;
+            fma2(x0, x1, s[c * 64 + 2 * x], s[c * 64 + 2 * x + 1], sl2, -m);
+            const float e0 = ex2(x0), e1 = ex2(x1);
+            add2(l0, l1, e0, e1);
+            pk[x] = DT<T>::pack2(e0, e1);
+          }
+          umma::st_32x32b_x32_u(t_lane + p_col + c * 32, pk);
+        }
+        if (rescale) {  // O_t is stable: P_t(g-1).V completed, P_t(g).V not released yet
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            float o[32];
+            umma::ld_32x32b_x32(t_lane + o_col + c * 32, o);
+            umma::ld_wait();
+#pragma unroll
+            for (int x = 0; x < 32; ++x) o[x] *= corr;
+            umma::st_32x32b_x32(t_lane + o_col + c * 32, o);
+          }
+        }
+        umma::st_wait();
+        umma::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&p_full[t]);
+      }
+      if (!ok) break;
+      // ---- item done: O (TMEM) / l -> out
+      ok = __all_sync(0xffffffffu, wait_or_abort(&pv_done[t], (g - 1) & 1, abort_flag, p.wait_ns));
+      if (!ok) break;
+      umma::fence_after_sync();
+      const float l = l0 + l1;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      T* orow = reinterpret_cast<T*>(p.out) + ((size_t)(it.s0 + q_pos) * p.n_heads + it.h0 + t) * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float o[32];
+        umma::ld_32x32b_x32(t_lane + o_col + c * 32, o);
+        umma::ld_wait();
+        if (q_pos < it.L) {
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8) {
+            uint4 w;
+            w.x = DT<T>::pack2(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv);
+            w.y = DT<T>::pack2(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv);
+            w.z = DT<T>::pack2(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv);
+            w.w = DT<T>::pack2(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + c8 * 8) = w;
+          }
+        }
+      }
+      umma::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&o_empty[t]);
+    }
+    if (!ok) report(p.status);
+  }
+
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    umma::fence_after_sync();
+    umma::tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+// -----------------------------------------------------------------------------
 // SIMT prefill (any dtype, head_dim 32/64/128): one warp handles four query
 // rows, lanes split head_dim, fp32 online softmax.  Also does the paged write.
 // -----------------------------------------------------------------------------
@@ -779,6 +1294,57 @@ int launch_tc(const PrefillParams& p, int total, int sched_capacity, CUtensorMap
   return TVK_OK;
 }
 
+template <typename T, int D>
+int launch_pair(const PrefillParams& p, int total, int sched_capacity, CUtensorMapDataType tdt, cudaStream_t stream) {
+  using C = PairCfg<D>;
+  CUtensorMap tq, tk, tv;
+  int rc = encode_rows_map(&tq, p.q, tdt, D, p.n_heads, total, 128);
+  if (rc == TVK_OK) rc = encode_rows_map(&tk, p.k, tdt, D, p.n_kv_heads, total, 128);
+  if (rc == TVK_OK) rc = encode_rows_map(&tv, p.v, tdt, D, p.n_kv_heads, total, 128);
+  if (rc != TVK_OK) return rc;
+  auto kern = flash_prefill_pair_kernel<T, D>;
+  static unsigned long long attr_mask = 0;
+  static int num_sms[64] = {0};
+  int dev = 0;
+  TVK_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev >= 64) {
+    tvk::set_error("device index %d beyond 63", dev);
+    return TVK_ERR_UNSUPPORTED;
+  }
+  if (!(attr_mask & (1ull << dev))) {
+    TVK_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));
+    // The warpgroups' register shares (setmaxnreg) must fit in what the launch provides.
+    cudaFuncAttributes fa;
+    TVK_CHECK_CUDA(cudaFuncGetAttributes(&fa, kern));
+    if (fa.numRegs < C::kRegsLaunchMin) {
+      tvk::set_error("prefill kernel built with %d registers per thread; its register split needs %d", fa.numRegs,
+                     C::kRegsLaunchMin);
+      return TVK_ERR_UNSUPPORTED;
+    }
+    TVK_CHECK_CUDA(cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev));
+    attr_mask |= 1ull << dev;
+  }
+  prefill_schedule_kernel<<<1, 1024, 0, stream>>>(p.cu_seqlens, p.n_seqs, p.n_mtiles, sched_capacity,
+                                                  const_cast<int32_t*>(p.sched), const_cast<int32_t*>(p.sched_count),
+                                                  p.ticket, p.status);
+  TVK_CHECK_LAUNCH("prefill_schedule");
+  const long long items = (long long)p.n_mtiles * p.n_seqs * (p.n_heads / 2);
+  const int grid = (int)(items < num_sms[dev] ? items : num_sms[dev]);  // one CTA per SM
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  TVK_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, p, tq, tk, tv));
+  TVK_CHECK_LAUNCH("flash_prefill_pair");
+  return TVK_OK;
+}
+
 template <typename T>
 int launch_simt(const PrefillParams& p, int max_seqlen, cudaStream_t stream) {
   dim3 grid((max_seqlen + kSimtRows - 1) / kSimtRows, p.n_heads, p.n_seqs);
@@ -791,7 +1357,17 @@ int launch_simt(const PrefillParams& p, int max_seqlen, cudaStream_t stream) {
   return TVK_OK;
 }
 
+// Which tcgen05 kernel this thread's prefill calls use (tvk_prefill_select_kernel).
+thread_local int g_prefill_choice = 0;
+int tvk_prefill_kernel_choice() { return g_prefill_choice; }
+
 }  // namespace
+
+extern "C" int tvk_prefill_select_kernel(int choice) {
+  TVK_CHECK_ARG(choice == 0 || choice == 1, "kernel choice %d (0 automatic, 1 one-head kernel)", choice);
+  g_prefill_choice = choice;
+  return TVK_OK;
+}
 
 extern "C" size_t tvk_flash_prefill_workspace_size(int n_seqs, int total_tokens) {
   if (n_seqs < 0 || total_tokens < 0) return tvk::kWorkspaceHeader;
@@ -867,6 +1443,16 @@ extern "C" int tvk_flash_prefill_attention(const void* q, const void* k, const v
     p.sched = w32 + tvk::kWorkspaceHeader / 4;
     const int cap = (int)((need - tvk::kWorkspaceHeader) / 4);
     p.sched_cap = cap;
+    // Heads in pairs sharing a KV head: the paired kernel (one CTA per SM, both heads'
+    // softmax in flight); otherwise (one query head per KV head, or an odd group) the
+    // one-head kernel.
+    if (p.group % 2 == 0 && tvk_prefill_kernel_choice() != 1) {
+      if (dtype == TVK_DTYPE_F16)
+        return head_dim == 64 ? launch_pair<__half, 64>(p, total_tokens, cap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, s)
+                              : launch_pair<__half, 128>(p, total_tokens, cap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, s);
+      return head_dim == 64 ? launch_pair<__nv_bfloat16, 64>(p, total_tokens, cap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, s)
+                            : launch_pair<__nv_bfloat16, 128>(p, total_tokens, cap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, s);
+    }
     if (dtype == TVK_DTYPE_F16)
       return head_dim == 64 ? launch_tc<__half, 64>(p, total_tokens, cap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, s)
                             : launch_tc<__half, 128>(p, total_tokens, cap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, s);
