@@ -132,8 +132,11 @@ size_t tvk_flash_prefill_workspace_size(int n_seqs, int total_tokens);
  * calls on the calling thread: 0 (default) = automatic -- the paired-head kernel
  * (two query heads that share a KV head per CTA item, one CTA per SM) whenever
  * n_heads / n_kv_heads is even, else the one-head kernel; 1 = always the
- * one-head kernel.  Both compute the same function; this exists so tests and
- * timings can run either.  No counterpart in the reference.
+ * one-head kernel; 2, 3, 4 = the paired kernel (where it applies) computing
+ * 0, 2/8 or 3/8 of the softmax exponentials with a polynomial on the FMA pipe
+ * instead of the exponential unit.  All compute the same function to within
+ * one 16-bit rounding of P; this exists so tests and timings can run each.
+ * No counterpart in the reference.
  */
 int tvk_prefill_select_kernel(int choice);
 int tvk_flash_prefill_attention(const void* q, const void* k, const void* v, void* out,

@@ -280,3 +280,34 @@ def test_both_kernels_agree_on_config2(cuda):
     torch.cuda.synchronize()
     diff = (outs[0].float() - outs[1].float()).abs().max().item()
     assert diff <= 4e-3, diff
+
+
+@pytest.fixture(params=[2, 3, 4], ids=["paired_mufu", "paired_fma_2of8", "paired_fma_3of8"])
+def pair_variant(request, cuda):
+    """The paired kernel with 0, 2/8 and 3/8 of the softmax exponentials computed by
+    a polynomial on the FMA pipe instead of the exponential unit."""
+    from tinyvllm_b200 import _lib
+    lib = _lib.lib()
+    assert lib.tvk_prefill_select_kernel(request.param) == 0
+    yield request.param
+    assert lib.tvk_prefill_select_kernel(0) == 0
+
+
+@pytest.mark.parametrize("dtype,D,nkv", [(torch.float16, 64, 4), (torch.bfloat16, 64, 8), (torch.bfloat16, 128, 8)])
+def test_paired_variants_vs_oracle(cuda, pair_variant, dtype, D, nkv):
+    """Config 2's prompts plus a running-max ramp through every exponential variant."""
+    from tinyvllm_b200.attention import flash_prefill_attention_varlen
+    q, k, v, cu, lens = _config2_inputs(cuda, dtype, D=D, nkv=nkv)
+    out = flash_prefill_attention_varlen(q, k, v, cu, max(lens))
+    torch.cuda.synchronize()
+    for i in range(len(lens)):
+        a, b = int(cu[i]), int(cu[i + 1])
+        _check(out[a:b], _oracle(q[a:b], k[a:b], v[a:b]), dtype)
+    g = torch.Generator(device=cuda).manual_seed(91)
+    L = 600
+    ramp = (0.25 + torch.arange(L, device=cuda, dtype=torch.float32) / 48.0)[:, None, None]
+    q2 = _rand((L, 32, D), dtype, g, cuda)
+    k2 = (torch.randn(L, nkv, D, generator=g, device=cuda) * ramp).to(dtype)
+    v2 = _rand((L, nkv, D), dtype, g, cuda)
+    _check(_flash(q2, k2, v2), _oracle(q2, k2, v2), dtype)
+    _check(_flash(q2, k2, v2, causal=False), _oracle(q2, k2, v2, causal=False), dtype)

@@ -672,7 +672,52 @@ __device__ __forceinline__ void add2(float& a0, float& a1, float b0, float b1) {
   asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(Dd));
 }
 
-template <typename T, int D>
+// (a0, a1) + (b, b) on the paired fp32 pipe.
+__device__ __forceinline__ void add2s(float& d0, float& d1, float a0, float a1, float b) {
+  uint64_t A, B, Dd;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(A) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(B) : "f"(b));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(Dd) : "l"(A), "l"(B));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(Dd));
+}
+// (a0, a1) * (b0, b1) + (c, c) on the paired fp32 pipe.
+__device__ __forceinline__ void fma2v(float& d0, float& d1, float a0, float a1, float b0, float b1, float c) {
+  uint64_t A, B, Cc, Dd;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(A) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(B) : "f"(b0), "f"(b1));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(Cc) : "f"(c));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(Dd) : "l"(A), "l"(B), "l"(Cc));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(Dd));
+}
+
+// 2^x for two values on the FMA and integer pipes instead of the exponential unit
+// (which computes only 16 results per cycle per SM and bounds the softmax at
+// head_dim 64).  Range reduction: x = j + f with j = round(x), taken by adding and
+// subtracting 1.5 * 2^23, and f in [-1/2, 1/2]; 2^f from a cubic whose
+// coefficients were fitted here to 2^f on [-1/2, 1/2] by reweighted least squares
+// on the relative error (largest relative error 7.5e-5 in fp32, below half a
+// 16-bit ulp of P); 2^j enters through the exponent bits.  x is clamped to
+// [-125, 127] so that the exponent stays normal (2^-125 rounds to zero in P).
+__device__ __forceinline__ void exp2_fma(float& y0, float& y1, float x0, float x1) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x0 = fminf(fmaxf(x0, -125.f), 127.f);
+  x1 = fminf(fmaxf(x1, -125.f), 127.f);
+  float t0, t1, r0, r1, f0, f1, p0, p1;
+  add2s(t0, t1, x0, x1, kRound);  // 1.5 * 2^23 + round(x)
+  add2s(r0, r1, t0, t1, -kRound);  // round(x)
+  f0 = x0 - r0;
+  f1 = x1 - r1;
+  fma2v(p0, p1, f0, f1, 0.0551716573536396f, 0.0551716573536396f, 0.2426111400127411f);
+  fma2v(p0, p1, p0, p1, f0, f1, 0.6932609677314758f);
+  fma2v(p0, p1, p0, p1, f0, f1, 0.9999280571937561f);
+  const int j0 = __float_as_int(t0) - 0x4B400000, j1 = __float_as_int(t1) - 0x4B400000;
+  y0 = __int_as_float(__float_as_int(p0) + (j0 << 23));
+  y1 = __int_as_float(__float_as_int(p1) + (j1 << 23));
+}
+
+// EMU: of every 8 pairs of exponentials of a score row, those with index % 8 < EMU
+// are computed with exp2_fma, the rest on the exponential unit.
+template <typename T, int D, int EMU>
 __global__ void __launch_bounds__(384, 1)
     flash_prefill_pair_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tm_q,
                               const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
@@ -1007,13 +1052,6 @@ __global__ void __launch_bounds__(384, 1)
         const float mx = max3f(max3f(mp[0], mp[1], mp[2]), max3f(mp[3], mp[4], mp[5]), fmaxf(mp[6], mp[7]));
         float m_cand = fmaxf(m, mx * sl2);
         if (m_cand == -INFINITY) m_cand = 0.f;  // no visible key (a row past the prompt's end)
-        // P_t's columns (and, when P lives over S, nothing else) are rewritten below:
-        // the previous tile's P_t.V must have completed.
-        if (g > 0) {
-          ok = __all_sync(0xffffffffu, wait_or_abort(&pv_done[t], (g - 1) & 1, abort_flag, p.wait_ns));
-          if (!ok) break;
-          umma::fence_after_sync();
-        }
         // Lazy rescale: the stale max is kept unless the new one is 2^8 larger; O_t
         // itself is rescaled after P is stored (the scores are dead by then), still
         // before P_t.V is released to add to it.
@@ -1025,20 +1063,31 @@ __global__ void __launch_bounds__(384, 1)
           l1 *= corr;
           m = m_cand;
         }
-        // P = 2^(s*scale - m), packed to 16-bit pairs: the A operand of P.V
+        // P = 2^(s*scale - m), packed to 16-bit pairs in registers (the A operand of
+        // P.V); these exponentials overlap the previous tile's P_t.V.
+        uint32_t pk[64];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t pk[32];
-#pragma unroll
-          for (int x = 0; x < 32; ++x) {
-            float x0, x1;
-            fma2(x0, x1, s[c * 64 + 2 * x], s[c * 64 + 2 * x + 1], sl2, -m);
-            const float e0 = ex2(x0), e1 = ex2(x1);
-            add2(l0, l1, e0, e1);
-            pk[x] = DT<T>::pack2(e0, e1);
+        for (int x = 0; x < 64; ++x) {
+          float x0, x1;
+          fma2(x0, x1, s[2 * x], s[2 * x + 1], sl2, -m);
+          float e0, e1;
+          if ((x & 7) < EMU) {
+            exp2_fma(e0, e1, x0, x1);
+          } else {
+            e0 = ex2(x0);
+            e1 = ex2(x1);
           }
-          umma::st_32x32b_x32_u(t_lane + p_col + c * 32, pk);
+          add2(l0, l1, e0, e1);
+          pk[x] = DT<T>::pack2(e0, e1);
         }
+        // P_t's columns are rewritten now: the previous tile's P_t.V must have completed.
+        if (g > 0) {
+          ok = __all_sync(0xffffffffu, wait_or_abort(&pv_done[t], (g - 1) & 1, abort_flag, p.wait_ns));
+          if (!ok) break;
+          umma::fence_after_sync();
+        }
+        umma::st_32x32b_x32_u(t_lane + p_col, pk);
+        umma::st_32x32b_x32_u(t_lane + p_col + 32, pk + 32);
         if (rescale) {  // O_t is stable: P_t(g-1).V completed, P_t(g).V not released yet
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
@@ -1294,7 +1343,7 @@ int launch_tc(const PrefillParams& p, int total, int sched_capacity, CUtensorMap
   return TVK_OK;
 }
 
-template <typename T, int D>
+template <typename T, int D, int EMU>
 int launch_pair(const PrefillParams& p, int total, int sched_capacity, CUtensorMapDataType tdt, cudaStream_t stream) {
   using C = PairCfg<D>;
   CUtensorMap tq, tk, tv;
@@ -1302,7 +1351,7 @@ int launch_pair(const PrefillParams& p, int total, int sched_capacity, CUtensorM
   if (rc == TVK_OK) rc = encode_rows_map(&tk, p.k, tdt, D, p.n_kv_heads, total, 128);
   if (rc == TVK_OK) rc = encode_rows_map(&tv, p.v, tdt, D, p.n_kv_heads, total, 128);
   if (rc != TVK_OK) return rc;
-  auto kern = flash_prefill_pair_kernel<T, D>;
+  auto kern = flash_prefill_pair_kernel<T, D, EMU>;
   static unsigned long long attr_mask = 0;
   static int num_sms[64] = {0};
   int dev = 0;
@@ -1359,12 +1408,18 @@ int launch_simt(const PrefillParams& p, int max_seqlen, cudaStream_t stream) {
 
 // Which tcgen05 kernel this thread's prefill calls use (tvk_prefill_select_kernel).
 thread_local int g_prefill_choice = 0;
+// Share of the softmax exponentials the automatic choice moves to the FMA pipe
+// (eighths of the pairs), per head_dim.
+constexpr int kAutoEmu64 = 0;
+constexpr int kAutoEmu128 = 0;
 int tvk_prefill_kernel_choice() { return g_prefill_choice; }
 
 }  // namespace
 
 extern "C" int tvk_prefill_select_kernel(int choice) {
-  TVK_CHECK_ARG(choice == 0 || choice == 1, "kernel choice %d (0 automatic, 1 one-head kernel)", choice);
+  TVK_CHECK_ARG(choice >= 0 && choice <= 4,
+                "kernel choice %d (0 automatic, 1 one-head, 2-4 paired with 0, 2 or 3 eighths of the exponentials "
+                "on the FMA pipe)", choice);
   g_prefill_choice = choice;
   return TVK_OK;
 }
@@ -1446,12 +1501,23 @@ extern "C" int tvk_flash_prefill_attention(const void* q, const void* k, const v
     // Heads in pairs sharing a KV head: the paired kernel (one CTA per SM, both heads'
     // softmax in flight); otherwise (one query head per KV head, or an odd group) the
     // one-head kernel.
-    if (p.group % 2 == 0 && tvk_prefill_kernel_choice() != 1) {
-      if (dtype == TVK_DTYPE_F16)
-        return head_dim == 64 ? launch_pair<__half, 64>(p, total_tokens, cap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, s)
-                              : launch_pair<__half, 128>(p, total_tokens, cap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, s);
-      return head_dim == 64 ? launch_pair<__nv_bfloat16, 64>(p, total_tokens, cap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, s)
-                            : launch_pair<__nv_bfloat16, 128>(p, total_tokens, cap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, s);
+    const int choice = tvk_prefill_kernel_choice();
+    if (p.group % 2 == 0 && choice != 1) {
+      // share of the exponentials computed on the FMA pipe (eighths of the pairs)
+      const int emu = choice == 2 ? 0 : choice == 3 ? 2 : choice == 4 ? 3 : (head_dim == 64 ? kAutoEmu64 : kAutoEmu128);
+      const CUtensorMapDataType tdt = dtype == TVK_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+#define TVK_PAIR(TT, DD)                                                   \
+  switch (emu) {                                                           \
+    case 2: return launch_pair<TT, DD, 2>(p, total_tokens, cap, tdt, s);   \
+    case 3: return launch_pair<TT, DD, 3>(p, total_tokens, cap, tdt, s);   \
+    default: return launch_pair<TT, DD, 0>(p, total_tokens, cap, tdt, s);  \
+  }
+      if (dtype == TVK_DTYPE_F16) {
+        if (head_dim == 64) { TVK_PAIR(__half, 64) } else { TVK_PAIR(__half, 128) }
+      } else {
+        if (head_dim == 64) { TVK_PAIR(__nv_bfloat16, 64) } else { TVK_PAIR(__nv_bfloat16, 128) }
+      }
+#undef TVK_PAIR
     }
     if (dtype == TVK_DTYPE_F16)
       return head_dim == 64 ? launch_tc<__half, 64>(p, total_tokens, cap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, s)
