@@ -775,6 +775,7 @@ def engine5_line(args, rank: int, world: int, local_rank: int):
         time.sleep(0.3)
     dist.barrier(device_ids=[local_rank])
     n0 = sum(len(r.tokens) for r in sharded.requests.values())
+    x0 = sharded.exchange_seconds
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
     ev0.record()
@@ -788,10 +789,12 @@ def engine5_line(args, rank: int, world: int, local_rank: int):
     made = sum(len(r.tokens) for r in sharded.requests.values()) - n0
     running = [s for s in eng.scheduler.running.values()]
     ctx_sum = sum(s.get_len() for s in running)
-    stats = torch.tensor([ev0.elapsed_time(ev1) / 1e3, wall, resident, ctx_sum], dtype=torch.float64, device=dev)
-    allst = torch.empty(world * 4, dtype=torch.float64, device=dev)
+    xchg = sharded.exchange_seconds - x0
+    stats = torch.tensor([ev0.elapsed_time(ev1) / 1e3, wall, resident, ctx_sum, xchg], dtype=torch.float64,
+                         device=dev)
+    allst = torch.empty(world * 5, dtype=torch.float64, device=dev)
     dist.all_gather_into_tensor(allst, stats)
-    allst = allst.view(world, 4).cpu().numpy()
+    allst = allst.view(world, 5).cpu().numpy()
     del eng._graphs
     if rank != 0:
         return None
@@ -818,6 +821,9 @@ def engine5_line(args, rank: int, world: int, local_rank: int):
         "timing": "device events around the timed engine steps, max over ranks (every step synchronises "
                   "the host); wall clock max over ranks beside it",
         "wall_ms_per_step": float(allst[:, 1].max()) / steps * 1e3,
+        "token_exchange_ms_per_step": float(allst[:, 4].max()) / steps * 1e3,
+        "token_exchange_note": "host wall time per step in ShardedEngine's exchange: the record's copy to the "
+                               "device, the NCCL all-gather and the copy back (max over ranks)",
         "clocks": clk,
     }
 

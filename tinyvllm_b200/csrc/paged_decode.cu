@@ -474,27 +474,34 @@ __global__ void __launch_bounds__(160, 2)
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
       mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      // Lazy rescale: the running max (and with it l and O) moves only when a row's
+      // new max exceeds it by more than 2^8, so P stays below 2^8 and most stages
+      // skip the O rescale.  The first processed stage always takes it (m = -inf).
       const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-      const float corr0 = exp2f(m0 - mn0), corr1 = exp2f(m1 - mn1);
-      m0 = mn0;
-      m1 = mn1;
+      if (__any_sync(0xffffffffu, mn0 > m0 + 8.f || mn1 > m1 + 8.f)) {
+        const float corr0 = ptx::ex2(m0 - mn0), corr1 = ptx::ex2(m1 - mn1);
+        m0 = mn0;
+        m1 = mn1;
+        l0 *= corr0;
+        l1 *= corr1;
+#pragma unroll
+        for (int i = 0; i < D / 8; ++i) {
+          o[i][0] *= corr0;
+          o[i][1] *= corr0;
+          o[i][2] *= corr1;
+          o[i][3] *= corr1;
+        }
+      }
       float pr[2][4];
 #pragma unroll
       for (int n = 0; n < 2; ++n) {
-        pr[n][0] = exp2f(sc[n][0] - mn0);
-        pr[n][1] = exp2f(sc[n][1] - mn0);
-        pr[n][2] = exp2f(sc[n][2] - mn1);
-        pr[n][3] = exp2f(sc[n][3] - mn1);
+        pr[n][0] = ptx::ex2(sc[n][0] - m0);
+        pr[n][1] = ptx::ex2(sc[n][1] - m0);
+        pr[n][2] = ptx::ex2(sc[n][2] - m1);
+        pr[n][3] = ptx::ex2(sc[n][3] - m1);
       }
-      l0 = l0 * corr0 + (pr[0][0] + pr[0][1] + pr[1][0] + pr[1][1]);
-      l1 = l1 * corr1 + (pr[0][2] + pr[0][3] + pr[1][2] + pr[1][3]);
-#pragma unroll
-      for (int i = 0; i < D / 8; ++i) {
-        o[i][0] *= corr0;
-        o[i][1] *= corr0;
-        o[i][2] *= corr1;
-        o[i][3] *= corr1;
-      }
+      l0 += (pr[0][0] + pr[0][1]) + (pr[1][0] + pr[1][1]);
+      l1 += (pr[0][2] + pr[0][3]) + (pr[1][2] + pr[1][3]);
       uint32_t pa[4];
       pa[0] = DT<T>::pack2(pr[0][0], pr[0][1]);
       pa[1] = DT<T>::pack2(pr[0][2], pr[0][3]);

@@ -21,6 +21,7 @@ group timeout of the next collective.
 
 from __future__ import annotations
 
+import time
 from dataclasses import dataclass, field
 from typing import Any, Dict, List, Optional
 
@@ -78,6 +79,7 @@ class ShardedEngine:
             cap = int(t.item())
         self.capacity = cap
         self.steps = 0
+        self.exchange_seconds = 0.0   # host wall time spent in the per-step token exchange
 
     # ------------------------------------------------------------------ API
     def add_request(self, prompt, sampling_params, prefilled_first_token: Optional[int] = None) -> int:
@@ -122,7 +124,9 @@ class ShardedEngine:
             rec[0] = _ERROR
             rec[1] = 0
             rec[2] = 0
+        t0 = time.perf_counter()
         gathered = self._all_gather(torch.from_numpy(rec))
+        self.exchange_seconds += time.perf_counter() - t0
         self.steps += 1
         if err is not None:
             raise ShardError(f"rank {self.rank} failed at step {self.steps}: {err}") from err
