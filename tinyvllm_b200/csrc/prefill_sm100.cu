@@ -600,6 +600,11 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
 //               softmax in the log2 domain with a lazy O rescale, P packed to
 //               16-bit pairs into TMEM, row sums in fp32 registers; at the end
 //               of an item the same threads normalise O and store the rows.
+//               Warps 4+q and 8+q share scheduler q and its exponential unit
+//               (16 results per cycle per SM, the floor at head_dim 64); they
+//               take turns on it tile by tile (exp_turn barriers), so one head
+//               stores P and waits for its next scores while the other
+//               exponentiates, instead of both leaving the unit idle at once.
 // TMEM columns, head_dim 64:  S0 0-127, S1 128-255, P0 256-319, P1 320-383,
 //                              O0 384-447, O1 448-511 (P apart from S, so the
 //                              next S never waits for the previous P.V).
@@ -620,8 +625,8 @@ struct PairCfg {
   static constexpr int kBarOff = kVOff + kStages * kTileBytes;
   static constexpr int kItemSlots = 4;
   // q_full[QB], q_empty[QB], k_full[S], v_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2],
-  // pv_done[2], o_empty[2], final[3], item_full[4], item_empty[4]
-  static constexpr int kNumBars = 2 * kQBufs + 3 * kStages + 10 + 3 + 2 * kItemSlots;
+  // pv_done[2], o_empty[2], final[3], item_full[4], item_empty[4], exp_turn[4][2]
+  static constexpr int kNumBars = 2 * kQBufs + 3 * kStages + 10 + 3 + 2 * kItemSlots + 8;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kUsed = kMiscOff + 16 + 32 * kItemSlots;
   static constexpr int kSmemBytes = kUsed + 1024;
@@ -747,6 +752,8 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* final_bar = o_empty + 2;  // [3] one per MMA-issuing warp
   uint64_t* item_full = final_bar + 3;
   uint64_t* item_empty = item_full + C::kItemSlots;
+  // exp_turn[q][t]: head t's softmax warp on scheduler q may start its exponentials
+  uint64_t* exp_turn = item_empty + C::kItemSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + C::kMiscOff + 4);
   volatile int* item_ring = reinterpret_cast<volatile int*>(base + C::kMiscOff + 16);  // [slot][8]
@@ -778,6 +785,7 @@ __global__ void __launch_bounds__(384, 1)
       ptx::mbar_init(&item_full[i], 1);
       ptx::mbar_init(&item_empty[i], 11);  // the three MMA issuers and the eight softmax warps
     }
+    for (int i = 0; i < 8; ++i) ptx::mbar_init(&exp_turn[i], 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -1063,6 +1071,11 @@ __global__ void __launch_bounds__(384, 1)
           l1 *= corr;
           m = m_cand;
         }
+        // Wait for this head's turn on the exponential unit (head 0 goes first on
+        // every tile; the turn order only schedules the unit, results do not depend on it).
+        ok = __all_sync(0xffffffffu, wait_or_abort(&exp_turn[quarter * 2 + t], (g & 1) ^ (t ? 0u : 1u), abort_flag,
+                                                   p.wait_ns));
+        if (!ok) break;
         // P = 2^(s*scale - m), packed to 16-bit pairs in registers (the A operand of
         // P.V); these exponentials overlap the previous tile's P_t.V.
         uint32_t pk[64];
@@ -1080,6 +1093,8 @@ __global__ void __launch_bounds__(384, 1)
           add2(l0, l1, e0, e1);
           pk[x] = DT<T>::pack2(e0, e1);
         }
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&exp_turn[quarter * 2 + (t ^ 1)]);  // the other head's turn
         // P_t's columns are rewritten now: the previous tile's P_t.V must have completed.
         if (g > 0) {
           ok = __all_sync(0xffffffffu, wait_or_abort(&pv_done[t], (g - 1) & 1, abort_flag, p.wait_ns));
