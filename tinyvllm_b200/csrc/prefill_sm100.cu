@@ -585,7 +585,7 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
 // query heads per KV head).  One CTA per SM walks the heaviest-first item list;
 // an item is one 128-row query tile of a PAIR of query heads (h, h+1) that read
 // the same KV head, so every K/V tile is loaded once for both.  Keys come in
-// tiles of 128.  12 warps in three warpgroups:
+// tiles of 128.  16 warps in four warpgroups:
 //   warp 0      TMA producer: both heads' Q tiles once per item, then the K/V
 //               ring; copies the diagonal tile's landed K/V rows into their
 //               paged slots when the pair holds the KV group's first head.
@@ -598,13 +598,16 @@ __global__ void __launch_bounds__(192, PfCfg<D>::kCtasPerSm)
 //   warps 4-7   softmax of head h, warps 8-11 softmax of head h+1: one query
 //               row per thread, 128 scores per key tile in registers, online
 //               softmax in the log2 domain with a lazy O rescale, P packed to
-//               16-bit pairs into TMEM, row sums in fp32 registers; at the end
-//               of an item the same threads normalise O and store the rows.
+//               16-bit pairs into TMEM, row sums in fp32 registers handed to
+//               the epilogue warps at the end of an item.
 //               Warps 4+q and 8+q share scheduler q and its exponential unit
 //               (16 results per cycle per SM, the floor at head_dim 64); they
 //               take turns on it tile by tile (exp_turn barriers), so one head
 //               stores P and waits for its next scores while the other
 //               exponentiates, instead of both leaving the unit idle at once.
+//   warps 12-15 epilogue: once a head's last P.V of an item completes, O / l
+//               is read from TMEM and stored, while the softmax warps already
+//               work on the next item.
 // TMEM columns, head_dim 64:  S0 0-127, S1 128-255, P0 256-319, P1 320-383,
 //                              O0 384-447, O1 448-511 (P apart from S, so the
 //                              next S never waits for the previous P.V).
@@ -625,19 +628,21 @@ struct PairCfg {
   static constexpr int kBarOff = kVOff + kStages * kTileBytes;
   static constexpr int kItemSlots = 4;
   // q_full[QB], q_empty[QB], k_full[S], v_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2],
-  // pv_done[2], o_empty[2], final[3], item_full[4], item_empty[4], exp_turn[4][2]
-  static constexpr int kNumBars = 2 * kQBufs + 3 * kStages + 10 + 3 + 2 * kItemSlots + 8;
+  // pv_done[2], o_empty[2], final[3], item_full[4], item_empty[4], exp_turn[4][2], epi_ready[2]
+  static constexpr int kNumBars = 2 * kQBufs + 3 * kStages + 10 + 3 + 2 * kItemSlots + 8 + 2;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
-  static constexpr int kUsed = kMiscOff + 16 + 32 * kItemSlots;
+  static constexpr int kLOff = kMiscOff + 16 + 32 * kItemSlots;  // row sums for the epilogue [2][2][128]
+  static constexpr int kUsed = kLOff + 2 * 2 * 128 * 4;
   static constexpr int kSmemBytes = kUsed + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory per CTA");
   static constexpr bool kPAlias = D == 128;             // P written over the first half of its S
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr int kThreads = 384;
-  // register split (setmaxnreg): warpgroup 0 drops to kRegsLow, the two softmax
-  // warpgroups rise to kRegsHigh; the launch must provide 384 x kRegsLaunchMin.
-  static constexpr int kRegsLow = 56, kRegsHigh = 224;
-  static constexpr int kRegsLaunchMin = (128 * kRegsLow + 256 * kRegsHigh + kThreads - 1) / kThreads;
+  static constexpr int kThreads = 512;
+  // register split (setmaxnreg): warpgroup 0 drops to kRegsLow, the epilogue
+  // warpgroup to kRegsEpi, the two softmax warpgroups rise to kRegsHigh; the
+  // launch must provide 512 x kRegsLaunchMin.
+  static constexpr int kRegsLow = 56, kRegsEpi = 56, kRegsHigh = 192;
+  static constexpr int kRegsLaunchMin = (128 * kRegsLow + 128 * kRegsEpi + 256 * kRegsHigh + kThreads - 1) / kThreads;
 };
 
 __device__ __forceinline__ uint32_t pcol(int D, int t) {
@@ -723,7 +728,7 @@ __device__ __forceinline__ void exp2_fma(float& y0, float& y1, float x0, float x
 // EMU: of every 8 pairs of exponentials of a score row, those with index % 8 < EMU
 // are computed with exp2_fma, the rest on the exponential unit.
 template <typename T, int D, int EMU>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(512, 1)
     flash_prefill_pair_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tm_q,
                               const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
   using C = PairCfg<D>;
@@ -754,6 +759,10 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t* item_empty = item_full + C::kItemSlots;
   // exp_turn[q][t]: head t's softmax warp on scheduler q may start its exponentials
   uint64_t* exp_turn = item_empty + C::kItemSlots;
+  uint64_t* epi_ready = exp_turn + 8;  // [2] head t's item is complete: its rows' sums are in l_buf
+  // l_buf[item parity][head][row]: two items in flight, so a one-tile item's sums
+  // cannot overwrite those the epilogue has yet to read
+  float* l_buf = reinterpret_cast<float*>(base + C::kLOff);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + C::kMiscOff);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(base + C::kMiscOff + 4);
   volatile int* item_ring = reinterpret_cast<volatile int*>(base + C::kMiscOff + 16);  // [slot][8]
@@ -783,9 +792,10 @@ __global__ void __launch_bounds__(384, 1)
     for (int i = 0; i < 3; ++i) ptx::mbar_init(&final_bar[i], 1);
     for (int i = 0; i < C::kItemSlots; ++i) {
       ptx::mbar_init(&item_full[i], 1);
-      ptx::mbar_init(&item_empty[i], 11);  // the three MMA issuers and the eight softmax warps
+      ptx::mbar_init(&item_empty[i], 15);  // the three MMA issuers, eight softmax and four epilogue warps
     }
     for (int i = 0; i < 8; ++i) ptx::mbar_init(&exp_turn[i], 1);
+    for (int t = 0; t < 2; ++t) ptx::mbar_init(&epi_ready[t], 4);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -1007,6 +1017,59 @@ __global__ void __launch_bounds__(384, 1)
     }
     __syncwarp();
    }
+  } else if (warp >= 12) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(C::kRegsEpi));
+    // ====================== epilogue warps (O -> out) =======================
+    // Warp 12+q reads TMEM lane quarter q: for each item and head, once the
+    // head's last P.V has completed, O / l for its 32 rows go to global memory
+    // and O_t is released to the next item's first P.V.
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+    uint32_t g = 0, item_it = 0;
+    bool ok = true;
+    PairItem it;
+    while (ok) {
+      const int got = take_item(it, false);
+      ok = __all_sync(0xffffffffu, got >= 0);
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&item_empty[(n_seen - 1) % C::kItemSlots]);
+      if (got == 0) break;
+      g += pair_kv_tiles(p, it);  // g - 1: the item's last key tile
+      const int q_pos = it.mtile * 128 + r;
+      for (int t = 0; t < 2 && ok; ++t) {
+        ok = __all_sync(0xffffffffu, wait_or_abort(&epi_ready[t], item_it & 1, abort_flag, p.wait_ns) &&
+                                         wait_or_abort(&pv_done[t], (g - 1) & 1, abort_flag, p.wait_ns));
+        if (!ok) break;
+        umma::fence_after_sync();
+        const float l = l_buf[((item_it & 1) * 2 + t) * 128 + r];
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        T* orow = reinterpret_cast<T*>(p.out) + ((size_t)(it.s0 + q_pos) * p.n_heads + it.h0 + t) * D;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float o[32];
+          umma::ld_32x32b_x32(t_lane + ocol(D, t) + c * 32, o);
+          umma::ld_wait();
+          if (q_pos < it.L) {
+#pragma unroll
+            for (int c8 = 0; c8 < 4; ++c8) {
+              uint4 w;
+              w.x = DT<T>::pack2(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv);
+              w.y = DT<T>::pack2(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv);
+              w.z = DT<T>::pack2(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv);
+              w.w = DT<T>::pack2(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv);
+              *reinterpret_cast<uint4*>(orow + c * 32 + c8 * 8) = w;
+            }
+          }
+        }
+        umma::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&o_empty[t]);
+      }
+      ++item_it;
+    }
+    if (!ok) report(p.status);
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(C::kRegsHigh));
     // =========================== softmax warps ==============================
@@ -1016,6 +1079,7 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
     const uint32_t s_col = t ? 128u : 0u, p_col = pcol(D, t), o_col = ocol(D, t);
     const float sl2 = p.scale_log2;
+    uint32_t item_it = 0;  // items finished (l_buf slot parity)
     uint32_t g = 0;  // K/V tiles seen (S, P and P.V phases follow it)
     bool ok = true;
     PairItem it;
@@ -1120,33 +1184,14 @@ __global__ void __launch_bounds__(384, 1)
         if (lane == 0) ptx::mbar_arrive(&p_full[t]);
       }
       if (!ok) break;
-      // ---- item done: O (TMEM) / l -> out
-      ok = __all_sync(0xffffffffu, wait_or_abort(&pv_done[t], (g - 1) & 1, abort_flag, p.wait_ns));
-      if (!ok) break;
-      umma::fence_after_sync();
-      const float l = l0 + l1;
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      T* orow = reinterpret_cast<T*>(p.out) + ((size_t)(it.s0 + q_pos) * p.n_heads + it.h0 + t) * D;
-#pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        float o[32];
-        umma::ld_32x32b_x32(t_lane + o_col + c * 32, o);
-        umma::ld_wait();
-        if (q_pos < it.L) {
-#pragma unroll
-          for (int c8 = 0; c8 < 4; ++c8) {
-            uint4 w;
-            w.x = DT<T>::pack2(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv);
-            w.y = DT<T>::pack2(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv);
-            w.z = DT<T>::pack2(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv);
-            w.w = DT<T>::pack2(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + c8 * 8) = w;
-          }
-        }
-      }
-      umma::fence_before_sync();
+      // ---- item done: the row sums go to the epilogue warps, which write O / l
+      // once the last P.V completes; this warp moves on to the next item.  The
+      // slot written here was last read by the epilogue two items back, which had
+      // finished before that item's first P.V (and so our previous P store) ran.
+      l_buf[((item_it & 1) * 2 + t) * 128 + r] = l0 + l1;
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&o_empty[t]);
+      if (lane == 0) ptx::mbar_arrive(&epi_ready[t]);
+      ++item_it;
     }
     if (!ok) report(p.status);
   }
@@ -1425,8 +1470,8 @@ int launch_simt(const PrefillParams& p, int max_seqlen, cudaStream_t stream) {
 thread_local int g_prefill_choice = 0;
 // Share of the softmax exponentials the automatic choice moves to the FMA pipe
 // (eighths of the pairs), per head_dim.
-constexpr int kAutoEmu64 = 0;
-constexpr int kAutoEmu128 = 0;
+constexpr int kAutoEmu64 = 2;
+constexpr int kAutoEmu128 = 2;
 int tvk_prefill_kernel_choice() { return g_prefill_choice; }
 
 }  // namespace
