@@ -1470,8 +1470,8 @@ int launch_simt(const PrefillParams& p, int max_seqlen, cudaStream_t stream) {
 thread_local int g_prefill_choice = 0;
 // Share of the softmax exponentials the automatic choice moves to the FMA pipe
 // (eighths of the pairs), per head_dim.
-constexpr int kAutoEmu64 = 2;
-constexpr int kAutoEmu128 = 2;
+constexpr int kAutoEmu64 = 0;
+constexpr int kAutoEmu128 = 0;
 int tvk_prefill_kernel_choice() { return g_prefill_choice; }
 
 }  // namespace
