@@ -619,8 +619,7 @@ def prefill_line(args, rank: int, world: int, local_rank: int):
         "e2e": {"value": T / (e2e_ms / 1e3), "unit": "prompt tok/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
         "gpu_launches": 2 * steps,
-        "kernel_choice": "paired-head kernel, 2/8 of the exponentials on the FMA pipe" if hkv and 32 // hkv % 2 == 0
-                         else "one-head kernel",
+        "kernel_choice": "paired-head kernel" if hkv and (32 // hkv) % 2 == 0 else "one-head kernel",
     }
 
 

@@ -334,9 +334,18 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const T* __restr
   float bv = -INFINITY;
   int bi = 0x7fffffff;
   const int nvec = vec ? vocab / N : 0;  // 16-byte loads only when every row is 16-byte aligned
-  // Four independent 16-byte loads in flight per thread (the compare order does not
-  // matter: ties go to the lower index whatever the order).
+  // Four independent 16-byte loads in flight per thread, each feeding its own
+  // running (max, index) pair so that the compares form four short chains
+  // instead of one long one; the pairs merge at the end (ties go to the lower
+  // index whatever the visiting order).
   constexpr int U = 4;
+  float cv[U];
+  int ci[U];
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    cv[k] = -INFINITY;
+    ci[k] = 0x7fffffff;
+  }
   int i = threadIdx.x;
   for (; i + (U - 1) * (int)blockDim.x < nvec; i += U * blockDim.x) {
     uint4 u[U];
@@ -349,13 +358,19 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const T* __restr
 #pragma unroll
       for (int e = 0; e < N; ++e) {
         const float f = DT<T>::to_f(h[e]);
-        if (better(f, i0 + e, bv, bi)) {
-          bv = f;
-          bi = i0 + e;
+        if (better(f, i0 + e, cv[k], ci[k])) {
+          cv[k] = f;
+          ci[k] = i0 + e;
         }
       }
     }
   }
+#pragma unroll
+  for (int k = 0; k < U; ++k)
+    if (better(cv[k], ci[k], bv, bi)) {
+      bv = cv[k];
+      bi = ci[k];
+    }
   for (; i < nvec; i += blockDim.x) {
     float f[N];
     load_vec<T>(row + (size_t)i * N, f);
