@@ -449,6 +449,45 @@ def decode_headline(args, rank: int, world: int, local_rank: int):
     }
 
 
+def decode_engine_shape_line(args, rank: int, world: int, local_rank: int):
+    """The decode attention call the config-4 engine makes at full batch: 64
+    sequences x 32 query / 4 KV heads, head_dim 64, fp16, 64-block tables (the
+    reference's 1024-token cap), every context 1024 tokens.  One call per step
+    with L2 flushed before it (each engine layer reads its own pool); CUDA events
+    around each call.  For profiling and the engine-shape figures; not a headline."""
+    import torch
+    from tinyvllm_b200 import workloads
+    from tinyvllm_b200.attention import paged_decode_attention
+    dev = torch.device("cuda", local_rank)
+    case = workloads.decode_case(64, 32, 4, 64, 16, [1024] * 64, dtype=torch.float16, device=dev, seed=3, width=64)
+    out = torch.empty_like(case.q)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    args_call = (case.q, case.k_cache, case.v_cache, case.block_tables, case.context_lens, 32, 4, 64, 16)
+    for _ in range(args.warmup):
+        paged_decode_attention(*args_call, out=out)
+    torch.cuda.synchronize(dev)
+    ts = []
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        paged_decode_attention(*args_call, out=out)
+        b.record()
+        torch.cuda.synchronize(dev)
+        ts.append(a.elapsed_time(b))
+    if rank != 0:
+        return None
+    ms = statistics.median(ts)
+    alg = case.algorithmic_bytes()
+    peak, kind = _peaks()
+    return {"metric": "paged-decode attention, engine shape (64 seqs x 4 KV heads, D=64, ctx 1024)",
+            "value": 64 / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms, "steps": args.steps,
+            "warmup": args.warmup, "n_gpus": 1, "higher_is_better": True, "dtype": "f16", "data": "synthetic",
+            "roofline": {"bound": "hbm", "achieved": alg / (ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": alg / (ms / 1e3) / 1e9 / peak, "peak_kind": kind},
+            "config": {"workload": "decode attention at the config-4 engine shape", "l2": "flushed before each call"}}
+
+
 PREFILL_LENS = (1, 15, 16, 17, 128, 500, 1024, 2048)
 
 
@@ -662,7 +701,8 @@ def engine4_line(args, rank: int, world: int, local_rank: int):
     cfg = tinyllama_config("float16")
     model = Llama(cfg, device=dev, seed=1234 + 4 + rank)
     rng = np.random.default_rng(1238 + rank)
-    prompts = [rng.integers(3, 32000, size=int(rng.integers(32, 513))).tolist() for _ in range(64)]
+    n_req, max_tokens = args.e2e_requests, args.e2e_max_tokens
+    prompts = [rng.integers(3, 32000, size=int(rng.integers(32, 513))).tolist() for _ in range(n_req)]
     eng = LLMEngine(model, max_batch_size=64, num_blocks=4096, num_scheduler_steps=1, use_cuda_graphs=True)
     steps = args.engine_steps
     ctx_trace = []
@@ -672,7 +712,7 @@ def engine4_line(args, rank: int, world: int, local_rank: int):
         while i < len(prompts) or eng.has_unfinished():
             for _ in range(4):
                 if i < len(prompts):
-                    eng.add_request(prompts[i], SamplingParams(max_tokens=128))
+                    eng.add_request(prompts[i], SamplingParams(max_tokens=max_tokens))
                     i += 1
             if trace:
                 ctx_trace.append([s.get_len() for s in eng.scheduler.running.values()])
@@ -709,7 +749,7 @@ def engine4_line(args, rank: int, world: int, local_rank: int):
     cpu = None if args.no_cpu_baseline else e2e_cpu_baseline(model)
     del eng._graphs
     return {
-        "metric": "e2e decode tok/s (config 4: TinyLlama-1.1B fp16, 64 requests x 128 greedy tokens)",
+        "metric": f"e2e decode tok/s (config 4: TinyLlama-1.1B fp16, {n_req} requests x {max_tokens} greedy tokens)",
         "value": made / dev_s, "unit": "tok/s", "n_gpus": 1, "steps": steps, "warmup": 1,
         "ms_per_step": dev_s * 1e3 / steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "f16", "data": "synthetic (random-init weights N(0,0.02), random prompt ids)",
@@ -905,10 +945,13 @@ def main() -> int:
                     help="headline only: skip the nested prefill / engine configurations")
     ap.add_argument("--batch", type=int, default=256,
                     help="sequences per GPU (default 256 = config 3; smaller only for profiling captures)")
-    ap.add_argument("--workload", choices=["decode", "prefill", "e2e", "e2e8b"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "e2e", "e2e8b", "decode-engine-shape"],
+                    default="decode",
                     help="decode = config 3 headline (+ nested configurations); prefill = config 2 flash prefill; "
                          "e2e = config 4 TinyLlama engine; e2e8b = config 5 sharded Llama-3-8B-shape decode")
     ap.add_argument("--prefill-steps", type=int, default=20)
+    ap.add_argument("--e2e-requests", type=int, default=64, help="config-4 requests (64 = the configuration)")
+    ap.add_argument("--e2e-max-tokens", type=int, default=128, help="config-4 tokens per request (128 = the configuration)")
     ap.add_argument("--engine-steps", type=int, default=2, help="config-4 runs timed")
     ap.add_argument("--engine-steps-c5", type=int, default=20, help="config-5 engine steps timed")
     ap.add_argument("--prefill-lens", default=None,
@@ -930,6 +973,8 @@ def main() -> int:
         return run_single(args, rank, world, local_rank, engine4_line)
     if args.workload == "e2e8b":
         return run_single(args, rank, world, local_rank, engine5_line)
+    if args.workload == "decode-engine-shape":
+        return run_single(args, rank, world, local_rank, decode_engine_shape_line)
     return run_ours(args, rank, world, local_rank)
 
 

@@ -248,6 +248,28 @@ def test_argmax(cuda, dtype, vocab):
     assert out[0].item() == 5
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_argmax_ties_nans_and_infs(cuda, dtype):
+    """First index on ties wherever the equal values sit (one 16-byte vector, two
+    vectors of one thread, two threads); the first NaN wins a row that has one;
+    a row of -inf gives index 0 -- all as numpy's argmax (sampling.py:133-134)."""
+    from tinyvllm_b200.layers import greedy_argmax
+    vocab = 128256
+    g = _gen(cuda, 7)
+    logits = torch.randn(6, vocab, generator=g, device=cuda).to(dtype)
+    logits[0, 3] = logits[0, 1] = 50           # same 16-byte vector
+    logits[1, 8 * 512 + 2] = logits[1, 2] = 50  # same thread, two of its in-flight vectors
+    logits[2, 4000] = logits[2, 77] = 50        # different threads
+    logits[3, 20] = float("nan")
+    logits[3, 7] = float("nan")
+    logits[4] = float("-inf")
+    logits[5, -1] = float("nan")
+    out = greedy_argmax(logits).cpu().numpy()
+    assert out.tolist()[:5] == [1, 2, 77, 7, 0]
+    assert out[5] == vocab - 1
+    assert np.array_equal(out, oa.greedy_argmax(_np(logits)))
+
+
 def test_argmax_strided_rows(cuda):
     from tinyvllm_b200.layers import greedy_argmax
     x = torch.randn(8, 3, 4096, device=cuda, dtype=torch.float16)

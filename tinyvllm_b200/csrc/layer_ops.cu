@@ -341,6 +341,7 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const T* __restr
   constexpr int U = 4;
   float cv[U];
   int ci[U];
+  int nan_i = 0x7fffffff;  // first NaN seen by this thread's chains
 #pragma unroll
   for (int k = 0; k < U; ++k) {
     cv[k] = -INFINITY;
@@ -355,13 +356,15 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const T* __restr
     for (int k = 0; k < U; ++k) {
       const T* h = reinterpret_cast<const T*>(&u[k]);
       const int i0 = (i + k * blockDim.x) * N;
+      // Inside one chain the indices only grow, so a strict '>' keeps the first of
+      // equal values; NaNs never win a '>' and are tracked apart (first index).
 #pragma unroll
       for (int e = 0; e < N; ++e) {
         const float f = DT<T>::to_f(h[e]);
-        if (better(f, i0 + e, cv[k], ci[k])) {
-          cv[k] = f;
-          ci[k] = i0 + e;
-        }
+        const bool gt = f > cv[k];
+        cv[k] = gt ? f : cv[k];
+        ci[k] = gt ? i0 + e : ci[k];
+        if (f != f) nan_i = min(nan_i, i0 + e);
       }
     }
   }
@@ -371,6 +374,10 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const T* __restr
       bv = cv[k];
       bi = ci[k];
     }
+  if (nan_i != 0x7fffffff && better(__int_as_float(0x7fc00000), nan_i, bv, bi)) {
+    bv = __int_as_float(0x7fc00000);
+    bi = nan_i;
+  }
   for (; i < nvec; i += blockDim.x) {
     float f[N];
     load_vec<T>(row + (size_t)i * N, f);
