@@ -361,7 +361,8 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const T* __restr
 #pragma unroll
       for (int e = 0; e < N; ++e) {
         const float f = DT<T>::to_f(h[e]);
-        const bool gt = f > cv[k];
+        // a chain's first non-NaN value is always taken (so rows of -inf keep their first index)
+        const bool gt = (f > cv[k] || ci[k] == 0x7fffffff) && f == f;
         cv[k] = gt ? f : cv[k];
         ci[k] = gt ? i0 + e : ci[k];
         if (f != f) nan_i = min(nan_i, i0 + e);
