@@ -334,11 +334,11 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const T* __restr
   float bv = -INFINITY;
   int bi = 0x7fffffff;
   const int nvec = vec ? vocab / N : 0;  // 16-byte loads only when every row is 16-byte aligned
-  // Four independent 16-byte loads in flight per thread, each feeding its own
-  // running (max, index) pair so that the compares form four short chains
+  // Eight independent 16-byte loads in flight per thread, each feeding its own
+  // running (max, index) pair so that the compares form eight short chains
   // instead of one long one; the pairs merge at the end (ties go to the lower
   // index whatever the visiting order).
-  constexpr int U = 4;
+  constexpr int U = 8;
   float cv[U];
   int ci[U];
   int nan_i = 0x7fffffff;  // first NaN seen by this thread's chains
