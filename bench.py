@@ -508,6 +508,9 @@ def prefill_line(args, rank: int, world: int, local_rank: int):
     from tinyvllm_b200.block_manager import BlockManager
 
     dev = torch.device("cuda", local_rank)
+    from tinyvllm_b200 import _lib
+    choice = {"auto": 0, "one-head": 1, "paired": 2}[args.prefill_kernel]
+    _lib.check(_lib.lib().tvk_prefill_select_kernel(choice), "tvk_prefill_select_kernel")
     lens = tuple(int(x) for x in args.prefill_lens.split(",")) if args.prefill_lens else PREFILL_LENS
     hq, hkv, hd = 32, args.prefill_kv_heads, args.prefill_head_dim
     dt = torch.bfloat16 if args.prefill_dtype == "bf16" else torch.float16
@@ -629,7 +632,7 @@ def prefill_line(args, rank: int, world: int, local_rank: int):
         cpu = {"value": T / dt_cpu, "unit": "prompt tok/s", "cores": threads, "kind": "port",
                "sample": "all 8 config-2 prompts once, numpy restatement of llama.py:58-94"}
     traffic = None
-    tp = ROOT / "profiles" / "flash_prefill_tc_config2.traffic.json"
+    tp = ROOT / "profiles" / "flash_prefill_pair_config2.traffic.json"
     if is_cfg2 and tp.exists():
         traffic = json.loads(tp.read_text()).get("bytes_per_launch")
     exp_bound = 2.0 * 2 * 128 * 64 * hd / 512 * 148 * 1.965e9 / 1e12
@@ -658,7 +661,8 @@ def prefill_line(args, rank: int, world: int, local_rank: int):
         "e2e": {"value": T / (e2e_ms / 1e3), "unit": "prompt tok/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
         "gpu_launches": 2 * steps,
-        "kernel_choice": "paired-head kernel" if hkv and (32 // hkv) % 2 == 0 else "one-head kernel",
+        "kernel_choice": ("paired-head kernel" if (32 // hkv) % 2 == 0 and args.prefill_kernel != "one-head"
+                          else "one-head kernel"),
     }
 
 
@@ -959,6 +963,8 @@ def main() -> int:
     ap.add_argument("--prefill-head-dim", type=int, choices=[64, 128], default=64)
     ap.add_argument("--prefill-kv-heads", type=int, default=4, help="prefill workload: KV heads (32 query heads)")
     ap.add_argument("--prefill-dtype", choices=["fp16", "bf16"], default="fp16")
+    ap.add_argument("--prefill-kernel", choices=["auto", "one-head", "paired"], default="auto",
+                    help="prefill workload: which tcgen05 kernel (auto = paired where the heads per KV head are even)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
