@@ -428,6 +428,106 @@ __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const T* __restr
   }
 }
 
+// 16-bit logits: per 16-byte vector a packed max tree (NaN-propagating), one
+// compare with the thread's running max, and only when a vector holds a new
+// maximum (a few times per thread) a scan for its first index.  A vector whose
+// max is NaN records the thread's first NaN instead (NaN beats every value).
+// Comparing in the 16-bit type orders values exactly as comparing their fp32
+// conversions does.
+template <typename T> struct Pack2;
+template <> struct Pack2<__half> {
+  using type = __half2;
+};
+template <> struct Pack2<__nv_bfloat16> {
+  using type = __nv_bfloat162;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kArgmaxThreads) argmax16_kernel(const T* __restrict__ logits,
+                                                                  int32_t* __restrict__ out, int vocab,
+                                                                  long long row_stride) {
+  using T2 = typename Pack2<T>::type;
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const T* row = logits + blockIdx.x * row_stride;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff, nan_i = 0x7fffffff;
+  const int nvec = vocab / 8;
+  auto visit = [&](const uint4& u, int i0) {
+    const T2* w = reinterpret_cast<const T2*>(&u);
+    const T2 c = __hmax2_nan(__hmax2_nan(w[0], w[1]), __hmax2_nan(w[2], w[3]));
+    const float fm = DT<T>::to_f(__hmax_nan(c.x, c.y));
+    if (fm != fm) {  // a NaN in this vector: the thread's first NaN (vectors come in increasing order)
+      if (nan_i == 0x7fffffff) {
+        const T* h = reinterpret_cast<const T*>(&u);
+        for (int e = 7; e >= 0; --e)
+          if (DT<T>::to_f(h[e]) != DT<T>::to_f(h[e])) nan_i = i0 + e;
+      }
+    } else if (fm > bv || bi == 0x7fffffff) {  // new maximum (or the thread's first vector)
+      const T* h = reinterpret_cast<const T*>(&u);
+      int e0 = 7;
+      for (int e = 7; e >= 0; --e)
+        if (DT<T>::to_f(h[e]) == fm) e0 = e;
+      bv = fm;
+      bi = i0 + e0;
+    }
+  };
+  constexpr int U = 8;
+  int i = threadIdx.x;
+  for (; i + (U - 1) * (int)blockDim.x < nvec; i += U * blockDim.x) {
+    uint4 u[U];
+#pragma unroll
+    for (int k = 0; k < U; ++k) u[k] = __ldg(reinterpret_cast<const uint4*>(row + (size_t)(i + k * blockDim.x) * 8));
+#pragma unroll
+    for (int k = 0; k < U; ++k) visit(u[k], (i + k * blockDim.x) * 8);
+  }
+  for (; i < nvec; i += blockDim.x) visit(__ldg(reinterpret_cast<const uint4*>(row + (size_t)i * 8)), i * 8);
+  for (int j = nvec * 8 + threadIdx.x; j < vocab; j += blockDim.x) {  // tail of a row not a multiple of 8
+    const float f = DT<T>::to_f(row[j]);
+    if (f != f) {
+      nan_i = min(nan_i, j);
+    } else if (better(f, j, bv, bi)) {
+      bv = f;
+      bi = j;
+    }
+  }
+  // A NaN anywhere wins: carry it as the candidate value (better() ranks NaN first).
+  if (nan_i != 0x7fffffff) {
+    bv = __int_as_float(0x7fc00000);
+    bi = nan_i;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    bv = lane < nw ? sv[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (better(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+  }
+}
+
 int grid_for(long long work, int threads) {
   long long g = (work + threads - 1) / threads;
   const long long cap = 148LL * 16;
@@ -616,8 +716,15 @@ extern "C" int tvk_argmax(const void* logits, int32_t* out, int rows, int vocab,
   TVK_CHECK_ARG(logits && out, "null pointer argument");
   const int vec = aligned16(logits) && row_stride % vec_elems(dtype) == 0;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  TVK_DISPATCH(dtype,
-               argmax_kernel<T><<<rows, kArgmaxThreads, 0, s>>>((const T*)logits, out, vocab, row_stride, vec));
+  if (vec && dtype == TVK_DTYPE_F16) {
+    argmax16_kernel<__half><<<rows, kArgmaxThreads, 0, s>>>((const __half*)logits, out, vocab, row_stride);
+  } else if (vec && dtype == TVK_DTYPE_BF16) {
+    argmax16_kernel<__nv_bfloat16><<<rows, kArgmaxThreads, 0, s>>>((const __nv_bfloat16*)logits, out, vocab,
+                                                                    row_stride);
+  } else {
+    TVK_DISPATCH(dtype,
+                 argmax_kernel<T><<<rows, kArgmaxThreads, 0, s>>>((const T*)logits, out, vocab, row_stride, vec));
+  }
   TVK_CHECK_LAUNCH("argmax");
   return TVK_OK;
 }
