@@ -627,9 +627,9 @@ struct PairCfg {
   static constexpr int kVOff = kKOff + kStages * kTileBytes;
   static constexpr int kBarOff = kVOff + kStages * kTileBytes;
   static constexpr int kItemSlots = 4;
-  // q_full[QB], q_empty[QB], k_full[S], v_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2],
+  // q_full[QB], q_empty[QB], k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[2], s_free[2], p_full[2],
   // pv_done[2], o_empty[2], final[3], item_full[4], item_empty[4], exp_turn[4][2], epi_ready[2]
-  static constexpr int kNumBars = 2 * kQBufs + 3 * kStages + 10 + 3 + 2 * kItemSlots + 8 + 2;
+  static constexpr int kNumBars = 2 * kQBufs + 4 * kStages + 10 + 3 + 2 * kItemSlots + 8 + 2;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kLOff = kMiscOff + 16 + 32 * kItemSlots;  // row sums for the epilogue [2][2][128]
   static constexpr int kUsed = kLOff + 2 * 2 * 128 * 4;
@@ -748,8 +748,12 @@ __global__ void __launch_bounds__(512, 1)
   uint64_t* q_empty = q_full + QB;
   uint64_t* k_full = q_empty + QB;
   uint64_t* v_full = k_full + S;
-  uint64_t* kv_empty = v_full + S;
-  uint64_t* s_full = kv_empty + S;  // [2] per head
+  // K(g) is released once both heads' S(g) are done, V(g) once both P.V are: the
+  // producer's K loads then run well ahead of the S MMAs instead of waiting for
+  // the later P.V of the same tile.
+  uint64_t* k_empty = v_full + S;
+  uint64_t* v_empty = k_empty + S;
+  uint64_t* s_full = v_empty + S;  // [2] per head
   uint64_t* s_free = s_full + 2;
   uint64_t* p_full = s_free + 2;
   uint64_t* pv_done = p_full + 2;
@@ -780,7 +784,8 @@ __global__ void __launch_bounds__(512, 1)
     for (int s = 0; s < S; ++s) {
       ptx::mbar_init(&k_full[s], 1);
       ptx::mbar_init(&v_full[s], 1);
-      ptx::mbar_init(&kv_empty[s], 3);  // the S issuer and both P.V issuers
+      ptx::mbar_init(&k_empty[s], 1);  // the S issuer
+      ptx::mbar_init(&v_empty[s], 2);  // both P.V issuers
     }
     for (int t = 0; t < 2; ++t) {
       ptx::mbar_init(&s_full[t], 1);
@@ -876,14 +881,18 @@ __global__ void __launch_bounds__(512, 1)
       for (int j = 0; j < n_kv; ++j, ++kv_it) {
         const int st = kv_it % S;
         const uint32_t ph = (kv_it / S) & 1;
-        ok = __all_sync(0xffffffffu, wait_or_abort(&kv_empty[st], ph ^ 1, abort_flag, p.wait_ns));
-        if (!ok) break;
         uint8_t* ks = base + C::kKOff + st * C::kTileBytes;
         uint8_t* vs = base + C::kVOff + st * C::kTileBytes;
+        ok = __all_sync(0xffffffffu, wait_or_abort(&k_empty[st], ph ^ 1, abort_flag, p.wait_ns));
+        if (!ok) break;
         if (lane == 0) {
           ptx::mbar_arrive_expect_tx(&k_full[st], C::kTileBytes);
           for (int kb = 0; kb < C::kKB; ++kb)
             tma_load_3d(ks + kb * C::kBlockBytes, &tm_k, &k_full[st], kb * 64, kvh, it.s0 + j * 128);
+        }
+        ok = __all_sync(0xffffffffu, wait_or_abort(&v_empty[st], ph ^ 1, abort_flag, p.wait_ns));
+        if (!ok) break;
+        if (lane == 0) {
           ptx::mbar_arrive_expect_tx(&v_full[st], C::kTileBytes);
           for (int kb = 0; kb < C::kKB; ++kb)
             tma_load_3d(vs + kb * C::kBlockBytes, &tm_v, &v_full[st], kb * 64, kvh, it.s0 + j * 128);
@@ -967,7 +976,7 @@ __global__ void __launch_bounds__(512, 1)
             umma::commit(&s_full[t]);
           }
           if (!ok) break;
-          umma::commit(&kv_empty[g % S]);                 // K(g) consumed
+          umma::commit(&k_empty[g % S]);                  // K(g) consumed
           if (j == n_kv - 1) umma::commit(&q_empty[qb]);  // Q is free once the item's S MMAs are done
         }
         ++q_it;
@@ -1007,7 +1016,7 @@ __global__ void __launch_bounds__(512, 1)
             umma::mma_f16_ts(tmem + ocol(D, t), tmem + pcol(D, t) + ks * 8, bd, idesc_o, (j == 0 && ks == 0) ? 0u : 1u);
           }
           umma::commit(&pv_done[t]);
-          umma::commit(&kv_empty[g % S]);  // V(g) consumed by this head
+          umma::commit(&v_empty[g % S]);  // V(g) consumed by this head
         }
         ++item_it;
       }
