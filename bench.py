@@ -924,6 +924,52 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> int:
     return 0
 
 
+def unit_probes_line(args, rank: int, world: int, local_rank: int):
+    """The two on-chip rates that bound the prefill kernels, measured by the
+    library's probes (tinyvllm_b200/csrc/probe_units.cu), one CTA per SM:
+    cycles per tcgen05.mma issued back to back by one thread (M = 128, K = 16,
+    N = 64 / 128 / 256) against the N-proportional ideal of 8,192 dense
+    FLOP per clock per SM, and exponentials per clock per SM for each ex2 form and
+    for the softmax's step per score pair.  Medians over CTAs; not a headline."""
+    import numpy as np
+    import torch
+    from tinyvllm_b200 import _lib
+    dev = torch.device("cuda", local_rank)
+    lib = _lib.lib()
+    n_sm = torch.cuda.get_device_properties(dev).multi_processor_count
+    out = torch.zeros(2 * n_sm, dtype=torch.int64, device=dev)
+    sink = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    mma = {}
+    n_mma = 4096
+    for n in (64, 128, 256):
+        for _ in range(2):  # the first round warms up
+            _lib.check(lib.tvk_probe_mma_issue(n, n_mma, out.data_ptr(), n_sm, stream), "tvk_probe_mma_issue")
+        torch.cuda.synchronize(dev)
+        c = out.view(n_sm, 2).cpu().numpy()
+        if (c[:, 1] < 0).any():
+            raise RuntimeError("an MMA probe CTA gave up waiting for completion")
+        ideal = 128 * n * 16 * 2 / 8192.0  # cycles per MMA at 8,192 FLOP per clock per SM
+        mma[f"n{n}"] = {"issue_cycles_per_mma": round(float(np.median(c[:, 0])) / n_mma, 1),
+                        "complete_cycles_per_mma": round(float(np.median(c[:, 1])) / n_mma, 1),
+                        "ideal_cycles_per_mma": ideal}
+    forms = {0: ("ex2.approx.ftz.f32", 1), 1: ("ex2.approx.f16x2", 2), 2: ("ex2.approx.ftz.bf16x2", 2),
+             3: ("softmax step per score pair (f32x2 fma, 2 ex2.f32, f32x2 add, f16x2 pack)", 2)}
+    exp = {}
+    n_iter = 2048
+    for form, (name, per_op) in forms.items():
+        for _ in range(2):
+            _lib.check(lib.tvk_probe_exp_unit(form, n_iter, out.data_ptr(), n_sm, sink.data_ptr(), stream),
+                       "tvk_probe_exp_unit")
+        torch.cuda.synchronize(dev)
+        cyc = float(np.median(out[:n_sm].cpu().numpy()))
+        ops = n_iter * 8 * 512  # per SM
+        exp[name] = {"exponentials_per_clock_per_sm": round(ops * per_op / cyc, 2)}
+    return {"metric": "on-chip unit rates (probes)", "n_gpus": 1, "data": "synthetic (zero operands)",
+            "config": {"workload": "unit-probes", "sms": n_sm, "mma_per_cta": n_mma, "exp_rounds": n_iter},
+            "tcgen05_mma_one_issuer": mma, "exp_unit": exp}
+
+
 def run_single(args, rank: int, world: int, local_rank: int, fn) -> int:
     import torch
     import torch.distributed as dist
@@ -949,7 +995,7 @@ def main() -> int:
                     help="headline only: skip the nested prefill / engine configurations")
     ap.add_argument("--batch", type=int, default=256,
                     help="sequences per GPU (default 256 = config 3; smaller only for profiling captures)")
-    ap.add_argument("--workload", choices=["decode", "prefill", "e2e", "e2e8b", "decode-engine-shape"],
+    ap.add_argument("--workload", choices=["decode", "prefill", "e2e", "e2e8b", "decode-engine-shape", "unit-probes"],
                     default="decode",
                     help="decode = config 3 headline (+ nested configurations); prefill = config 2 flash prefill; "
                          "e2e = config 4 TinyLlama engine; e2e8b = config 5 sharded Llama-3-8B-shape decode")
@@ -981,6 +1027,8 @@ def main() -> int:
         return run_single(args, rank, world, local_rank, engine5_line)
     if args.workload == "decode-engine-shape":
         return run_single(args, rank, world, local_rank, decode_engine_shape_line)
+    if args.workload == "unit-probes":
+        return run_single(args, rank, world, local_rank, unit_probes_line)
     return run_ours(args, rank, world, local_rank)
 
 

@@ -309,6 +309,23 @@ int tvk_debug_arm_wait_timeout(long long limit_ns);
 int tvk_selftest_umma_gemm(const void* a, const void* b, float* c, int n, int k, int b_mn_major,
                            int a_in_tmem, int dtype, int* status, void* stream);
 
+/*
+ * Measurement probes (no reference counterpart; nothing on the attention path
+ * uses them).  One CTA per SM for n_ctas CTAs (use the SM count), cycles from
+ * clock64, written to device memory `out`:
+ *   tvk_probe_mma_issue: one thread issues n_mma tcgen05.mma.cta_group::1
+ *     kind::f16 (M = 128, N = n in {64, 128, 256}, K = 16, zero bf16 operands
+ *     in shared memory) back to back; out[2c] = cycles of CTA c's issue loop,
+ *     out[2c + 1] = cycles until the last MMA completed (-1: wait gave up).
+ *   tvk_probe_exp_unit: 16 warps per SM run 8 dependent chains each per thread
+ *     for n_iter rounds of one form -- 0 ex2.approx.ftz.f32, 1 ex2.approx.f16x2,
+ *     2 ex2.approx.ftz.bf16x2, 3 the prefill softmax step per score pair (f32x2
+ *     FMA, two f32 ex2, f32x2 add, f16x2 pack); out[c] = cycles.  `sink` is a
+ *     4-byte device scratch word.
+ */
+int tvk_probe_mma_issue(int n, int n_mma, long long* out, int n_ctas, void* stream);
+int tvk_probe_exp_unit(int form, int n_iter, long long* out, int n_ctas, void* sink, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -138,3 +138,11 @@ def test_wait_test_hook_rejects_limits_out_of_range(lib):
 
 def test_noalloc_status_rejects_null(lib):
     assert lib.tvk_paged_decode_noalloc_status(None, None) == -1
+
+
+def test_probes_reject_bad_arguments(lib):
+    # argument checks run before any CUDA call
+    assert lib.tvk_probe_mma_issue(96, 16, None, 1, None) != 0
+    assert lib.tvk_probe_mma_issue(128, 16, None, 1, None) != 0
+    assert lib.tvk_probe_exp_unit(7, 16, None, 1, None, None) != 0
+    assert lib.tvk_probe_exp_unit(0, 0, None, 1, None, None) != 0

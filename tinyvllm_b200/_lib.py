@@ -50,6 +50,8 @@ SIGNATURES = {
         _c_int,
         [_c_void] * 5 + [_c_int] * 8 + [_c_void] * 3 + [_c_int] * 2 + [_c_void, _c_size, _c_void],
     ),
+    "tvk_probe_mma_issue": (_c_int, [_c_int, _c_int, _c_void, _c_int, _c_void]),
+    "tvk_probe_exp_unit": (_c_int, [_c_int, _c_int, _c_void, _c_int, _c_void, _c_void]),
 }
 
 _lib = None
