@@ -166,6 +166,11 @@ def test_rms_norm_write_kv_matches_separate_ops(cuda, dtype, hkv, d):
     write_kv_slots(k, v, slots, kc1, vc1)
     out2 = rms_norm(x, w, 1e-5, residual=r2, write_kv=(k, v, slots, kc2, vc2))
     torch.cuda.synchronize()
+    # against the oracle directly: the stored residual sum is the dtype-rounded
+    # x + r (llama.py:248), the output rms_norm of it (llama.py:14-23)
+    s_ref = (x.float() + r.float()).to(dtype)
+    assert torch.equal(r2, s_ref)
+    _check(out2, oa.rms_norm(_np(s_ref), _np(w), 1e-5), dtype, scale=4)
     assert torch.equal(out1, out2) and torch.equal(r1, r2)
     assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2)
     flat_k, flat_v = kc2.view(-1, hkv, d), vc2.view(-1, hkv, d)
@@ -191,6 +196,18 @@ def test_qkv_rope_matches_separate_ops(cuda, dtype, with_slots):
     kc = torch.zeros(4, 16, hkv, d, dtype=dtype, device=cuda)
     vc = torch.zeros_like(kc)
     q, k, v = qkv_rope(qkv, hq, hkv, d, cos, sin, pos, slots=slots, k_cache=kc, v_cache=vc)
+    torch.cuda.synchronize()
+    # against the oracle directly: split of the packed projection row, RoPE of q
+    # and k with the per-token table rows (llama.py:26-55, :316-326)
+    c_ref, s_ref = oa.precompute_freqs_cis(d, 1024, 5e5)
+    pn = pos.cpu().numpy()
+    qkv_n = _np(qkv)
+    q_n = qkv_n[:, :hq * d].reshape(T, hq, d)
+    k_n = qkv_n[:, hq * d:(hq + hkv) * d].reshape(T, hkv, d)
+    v_n = qkv_n[:, (hq + hkv) * d:].reshape(T, hkv, d)
+    _check(q, oa.apply_rope(q_n[:, None], c_ref[pn][:, None], s_ref[pn][:, None])[:, 0], dtype, scale=2)
+    _check(k, oa.apply_rope(k_n[:, None], c_ref[pn][:, None], s_ref[pn][:, None])[:, 0], dtype, scale=2)
+    assert np.array_equal(_np(v), v_n)
     q2 = qkv[:, :hq * d].reshape(T, hq, d).contiguous()
     k2 = qkv[:, hq * d:(hq + hkv) * d].reshape(T, hkv, d).contiguous()
     v2 = qkv[:, (hq + hkv) * d:].reshape(T, hkv, d).contiguous()

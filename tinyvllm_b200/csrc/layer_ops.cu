@@ -72,7 +72,8 @@ struct KvAppend {
   long long n_slots;   // num_blocks * block_size
 };
 
-template <typename T>
+// VPT: vectors per thread the row needs (ceil(dim / N / kNormThreads), 1/2/4/8).
+template <typename T, int VPT>
 __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const T* __restrict__ x, const T* residual,
                                                                 T* residual_out, const T* __restrict__ w,
                                                                 T* __restrict__ out, int dim, float eps,
@@ -80,27 +81,20 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const T* __restr
   constexpr int N = Vec<T>::N;
   __shared__ float red[32];
   const size_t row = blockIdx.x;
-  if (kv.slots) {
-    // This row's new k and v rows go to its paged slot (decode append done
-    // after the attention that read the slot's old contents).
-    const long long slot = kv.slots[row];
-    if (slot >= 0 && slot < kv.n_slots) {
-      for (int i = threadIdx.x; i < kv.row_elems / N; i += kNormThreads) {
-        const size_t src = row * kv.row_elems + (size_t)i * N, dst = (size_t)slot * kv.row_elems + (size_t)i * N;
-        *reinterpret_cast<uint4*>(kv.k_cache + dst) = *reinterpret_cast<const uint4*>(kv.k + src);
-        *reinterpret_cast<uint4*>(kv.v_cache + dst) = *reinterpret_cast<const uint4*>(kv.v + src);
-      }
-    }
-  }
+  // Every load this row needs is issued up front (the slot of the K/V append,
+  // the row, the residual and the weight), so their latencies overlap instead of
+  // following the reduction.
+  const long long slot = kv.slots ? kv.slots[row] : -1;
   const T* xr = x + row * dim;
   const int nvec = dim / N;
-  float v[kNormMaxVec][N];
+  float v[VPT][N], wv[VPT][N];
   float ss = 0.f;
 #pragma unroll
-  for (int k = 0; k < kNormMaxVec; ++k) {
+  for (int k = 0; k < VPT; ++k) {
     const int i = threadIdx.x + k * kNormThreads;
     if (i < nvec) {
       load_vec<T>(xr + i * N, v[k]);
+      load_vec<T>(w + i * N, wv[k]);
       if (residual) {
         float rv[N];
         load_vec<T>(residual + row * dim + i * N, rv);
@@ -112,16 +106,24 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const T* __restr
       for (int e = 0; e < N; ++e) ss = fmaf(v[k][e], v[k][e], ss);
     }
   }
+  if (kv.slots && slot >= 0 && slot < kv.n_slots) {
+    // This row's new k and v rows go to its paged slot (decode append done
+    // after the attention that read the slot's old contents).
+    for (int i = threadIdx.x; i < kv.row_elems / N; i += kNormThreads) {
+      const size_t src = row * kv.row_elems + (size_t)i * N, dst = (size_t)slot * kv.row_elems + (size_t)i * N;
+      *reinterpret_cast<uint4*>(kv.k_cache + dst) = *reinterpret_cast<const uint4*>(kv.k + src);
+      *reinterpret_cast<uint4*>(kv.v_cache + dst) = *reinterpret_cast<const uint4*>(kv.v + src);
+    }
+  }
   const float tot = block_sum(ss, red);
   const float inv = rsqrtf(tot / (float)dim + eps);
 #pragma unroll
-  for (int k = 0; k < kNormMaxVec; ++k) {
+  for (int k = 0; k < VPT; ++k) {
     const int i = threadIdx.x + k * kNormThreads;
     if (i < nvec) {
-      float wv[N], o[N];
-      load_vec<T>(w + i * N, wv);
+      float o[N];
 #pragma unroll
-      for (int e = 0; e < N; ++e) o[e] = v[k][e] * inv * wv[e];
+      for (int e = 0; e < N; ++e) o[e] = v[k][e] * inv * wv[k][e];
       store_vec<T>(out + row * dim + i * N, o);
     }
   }
@@ -546,6 +548,16 @@ bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
 int vec_elems(int dtype) { return dtype == TVK_DTYPE_F32 ? 4 : 8; }
 
+template <typename T>
+void launch_rms_norm(int rows, int dim, cudaStream_t s, const T* x, const T* residual, T* residual_out, const T* w,
+                     T* out, float eps, const KvAppend<T>& kv) {
+  const int vpt = (dim / Vec<T>::N + kNormThreads - 1) / kNormThreads;
+  if (vpt <= 1) rms_norm_kernel<T, 1><<<rows, kNormThreads, 0, s>>>(x, residual, residual_out, w, out, dim, eps, kv);
+  else if (vpt <= 2) rms_norm_kernel<T, 2><<<rows, kNormThreads, 0, s>>>(x, residual, residual_out, w, out, dim, eps, kv);
+  else if (vpt <= 4) rms_norm_kernel<T, 4><<<rows, kNormThreads, 0, s>>>(x, residual, residual_out, w, out, dim, eps, kv);
+  else rms_norm_kernel<T, kNormMaxVec><<<rows, kNormThreads, 0, s>>>(x, residual, residual_out, w, out, dim, eps, kv);
+}
+
 }  // namespace
 
 extern "C" int tvk_rms_norm(const void* x, const void* residual, void* residual_out, const void* weight, void* out,
@@ -561,8 +573,8 @@ extern "C" int tvk_rms_norm(const void* x, const void* residual, void* residual_
   TVK_CHECK_ARG(aligned16(x) && aligned16(weight) && aligned16(out) && (!residual || (aligned16(residual) &&
                 aligned16(residual_out))), "pointers must be 16-byte aligned");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  TVK_DISPATCH(dtype, rms_norm_kernel<T><<<rows, kNormThreads, 0, s>>>(
-      (const T*)x, (const T*)residual, (T*)residual_out, (const T*)weight, (T*)out, dim, eps, KvAppend<T>{}));
+  TVK_DISPATCH(dtype, launch_rms_norm<T>(rows, dim, s, (const T*)x, (const T*)residual, (T*)residual_out,
+                                         (const T*)weight, (T*)out, eps, KvAppend<T>{}));
   TVK_CHECK_LAUNCH("rms_norm");
   return TVK_OK;
 }
@@ -586,10 +598,10 @@ extern "C" int tvk_rms_norm_write_kv(const void* x, const void* residual, void* 
                     (!residual || (aligned16(residual) && aligned16(residual_out))),
                 "pointers must be 16-byte aligned");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  TVK_DISPATCH(dtype, rms_norm_kernel<T><<<rows, kNormThreads, 0, s>>>(
-      (const T*)x, (const T*)residual, (T*)residual_out, (const T*)weight, (T*)out, dim, eps,
-      KvAppend<T>{(const T*)k, (const T*)v, slots, (T*)k_cache, (T*)v_cache, n_kv_heads * head_dim,
-                  (long long)num_blocks * block_size}));
+  TVK_DISPATCH(dtype, launch_rms_norm<T>(rows, dim, s, (const T*)x, (const T*)residual, (T*)residual_out,
+                                         (const T*)weight, (T*)out, eps,
+                                         KvAppend<T>{(const T*)k, (const T*)v, slots, (T*)k_cache, (T*)v_cache,
+                                                     n_kv_heads * head_dim, (long long)num_blocks * block_size}));
   TVK_CHECK_LAUNCH("rms_norm_write_kv");
   return TVK_OK;
 }
