@@ -90,6 +90,13 @@ def test_random_operation_sequences_match_oracle(seed):
                 b.free_sequence(s)
         finally:
             assert _state(a) == _state(b)
+            if live:  # the dense table mirror agrees with the oracle's lists at any width
+                w = int(rng.integers(1, 12))
+                exp = np.zeros((len(live), w), dtype=np.int32)
+                for i, sid in enumerate(live):
+                    t = b.block_tables[sid][:w]
+                    exp[i, :len(t)] = t
+                assert np.array_equal(a.block_table_array(live, w), exp)
 
 
 def test_slot_mapping_matches_chunked_prompt_writes():

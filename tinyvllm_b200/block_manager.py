@@ -14,7 +14,9 @@ kernels in one vectorised step instead of per-token Python loops:
   (``tinyvllm/model/llama.py:188-209``);
 * ``block_table_array(seq_ids, width)`` -- the padded ``int32 [B, width]``
   table of ``LLMEngine._prepare_batch_tensors`` (``core/engine.py:235-255``):
-  block 0 as padding, truncated at ``width``.
+  block 0 as padding, truncated at ``width``.  Every registered sequence also
+  owns a row of a dense int32 array that mirrors its block list (zeros past
+  its end), so a batch's table is one gather instead of a per-sequence copy.
 """
 
 from __future__ import annotations
@@ -35,12 +37,43 @@ class BlockManager:
         self.seq_to_gpu: Dict[int, int] = {}
         self.block_tables: Dict[int, List[int]] = {}
         self.seq_positions: Dict[int, int] = {}
+        # dense mirror of the block lists: one int32 row per registered sequence
+        self._rows = np.zeros((64, 64), dtype=np.int32)
+        self._row_of: Dict[int, int] = {}
+        self._free_rows: List[int] = list(range(63, -1, -1))
+
+    def _take_row(self, seq_id: int) -> int:
+        if not self._free_rows:
+            n = self._rows.shape[0]
+            self._rows = np.concatenate([self._rows, np.zeros_like(self._rows)], axis=0)
+            self._free_rows = list(range(2 * n - 1, n - 1, -1))
+        r = self._free_rows.pop()
+        self._row_of[seq_id] = r
+        return r
+
+    def _mirror(self, seq_id: int, start: int) -> None:
+        """Copy block-list entries from ``start`` on into the sequence's row."""
+        table = self.block_tables[seq_id]
+        if len(table) > self._rows.shape[1]:
+            w = self._rows.shape[1]
+            while w < len(table):
+                w *= 2
+            self._rows = np.pad(self._rows, ((0, 0), (0, w - self._rows.shape[1])))
+        self._rows[self._row_of[seq_id], start:len(table)] = table[start:]
 
     # -- reference API ---------------------------------------------------------
     def register_sequence(self, seq_id: int, gpu_id: int = 0) -> None:
+        if seq_id in self._row_of:           # re-registered: start from an empty row
+            self._release_row(seq_id)
         self.seq_to_gpu[seq_id] = gpu_id
         self.block_tables[seq_id] = []
         self.seq_positions[seq_id] = 0
+        self._take_row(seq_id)
+
+    def _release_row(self, seq_id: int) -> None:
+        r = self._row_of.pop(seq_id)
+        self._rows[r, :] = 0
+        self._free_rows.append(r)
 
     def ensure_block_for_position(self, seq_id: int, pos: int) -> int:
         table = self.block_tables[seq_id]
@@ -77,6 +110,7 @@ class BlockManager:
         del self.seq_to_gpu[seq_id]
         del self.block_tables[seq_id]
         del self.seq_positions[seq_id]
+        self._release_row(seq_id)
 
     def get_num_free_blocks(self, gpu_id: Optional[int] = None) -> int:
         if gpu_id is None:
@@ -91,6 +125,10 @@ class BlockManager:
         refs = self.ref_counts[gpu_id]
         for block_id in self.block_tables[src_seq_id]:
             refs[block_id] += 1
+        if dst_seq_id in self._row_of:
+            self._release_row(dst_seq_id)
+        self._take_row(dst_seq_id)
+        self._mirror(dst_seq_id, 0)
 
     # -- vectorised helpers for the kernels -------------------------------------
     def _grow(self, seq_id: int, n_blocks: int) -> None:
@@ -101,12 +139,17 @@ class BlockManager:
         gpu_id = self.seq_to_gpu[seq_id]
         free = self.free_blocks[gpu_id]
         refs = self.ref_counts[gpu_id]
-        while len(table) < n_blocks:
-            if not free:
-                raise RuntimeError("Out of KV cache memory!")
-            b = free.pop()
-            refs[b] = 1
-            table.append(b)
+        start = len(table)
+        try:
+            while len(table) < n_blocks:
+                if not free:
+                    raise RuntimeError("Out of KV cache memory!")
+                b = free.pop()
+                refs[b] = 1
+                table.append(b)
+        finally:
+            if seq_id in self._row_of and len(table) > start:
+                self._mirror(seq_id, start)
 
     def slot_mapping(self, seq_id: int, start_pos: int, n: int) -> np.ndarray:
         """int64 flat slots of positions ``start_pos .. start_pos+n-1``, allocating
@@ -124,14 +167,13 @@ class BlockManager:
                           out: Optional[np.ndarray] = None) -> np.ndarray:
         """int32 [len(seq_ids), width] tables padded with block 0 and truncated at
         ``width`` (default: the longest table)."""
-        tables = [self.block_tables[s] for s in seq_ids]
         if width is None:
-            width = max((len(t) for t in tables), default=1) or 1
+            width = max((len(self.block_tables[s]) for s in seq_ids), default=1) or 1
+        rows = np.fromiter((self._row_of[s] for s in seq_ids), dtype=np.int64, count=len(seq_ids))
+        w = min(width, self._rows.shape[1])
         if out is None:
-            out = np.zeros((len(tables), width), dtype=np.int32)
+            out = np.zeros((len(rows), width), dtype=np.int32)
         else:
-            out[:len(tables), :width] = 0
-        for i, t in enumerate(tables):
-            n = min(len(t), width)
-            out[i, :n] = t[:n]
+            out[:len(rows), :width] = 0
+        out[:len(rows), :w] = self._rows[rows, :w]
         return out
