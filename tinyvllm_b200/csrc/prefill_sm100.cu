@@ -41,7 +41,7 @@ struct PrefillParams {
   void* k_cache;
   void* v_cache;
   int* status;                  // may be null
-  const int32_t* sched;         // tc path: (seq << 16 | query tile) items, heaviest first
+  const int4* sched;            // tc path: {seq, query tile, first token, length} items, heaviest first
   const int32_t* sched_count;   // tc path: number of entries in sched
   int* ticket;                  // tc path: next item to hand out (zeroed by the schedule kernel)
   int n_seqs, n_heads, n_kv_heads, group, head_dim, causal, num_blocks, block_size, n_mtiles;
@@ -162,11 +162,9 @@ struct Item {
 // running its prologue); an entry that does not describe a query tile of a
 // prompt inside the token range comes back with seq = -1.
 __device__ __forceinline__ Item item_of(const PrefillParams& p, int w) {
-  const int e = __ldcg(p.sched + w / p.n_heads);
-  const int seq = e >> 16, m = e & 0xFFFF;
-  if (seq < 0 || seq >= p.n_seqs || m >= p.n_mtiles) return Item{-1, 0, 0, 0, 0};
-  const int s0 = __ldcg(p.cu_seqlens + seq);
-  const int L = __ldcg(p.cu_seqlens + seq + 1) - s0;
+  const int4 e = __ldcg(p.sched + w / p.n_heads);
+  const int seq = e.x, m = e.y, s0 = e.z, L = e.w;
+  if (seq < 0 || seq >= p.n_seqs || m < 0 || m >= p.n_mtiles) return Item{-1, 0, 0, 0, 0};
   if (s0 < 0 || L <= m * 128 || s0 + L > p.total_tokens) return Item{-1, 0, 0, 0, 0};
   return Item{seq, m, w % p.n_heads, s0, L};
 }
@@ -628,8 +626,8 @@ struct PairCfg {
   static constexpr int kBarOff = kVOff + kStages * kTileBytes;
   static constexpr int kItemSlots = 4;
   // q_full[QB], q_empty[QB], k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[2], s_free[2], p_full[2],
-  // pv_done[2], o_empty[2], final[3], item_full[4], item_empty[4], exp_turn[4][2], epi_ready[2]
-  static constexpr int kNumBars = 2 * kQBufs + 4 * kStages + 10 + 3 + 2 * kItemSlots + 8 + 2;
+  // pv_done[2], o_empty[2], final[3], item_full[4], item_empty[4], exp_turn[4][2], epi_ready[2][2]
+  static constexpr int kNumBars = 2 * kQBufs + 4 * kStages + 10 + 3 + 2 * kItemSlots + 8 + 4;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kLOff = kMiscOff + 16 + 32 * kItemSlots;  // row sums for the epilogue [2][2][128]
   static constexpr int kUsed = kLOff + 2 * 2 * 128 * 4;
@@ -659,11 +657,9 @@ struct PairItem {
 
 __device__ __forceinline__ PairItem pair_item_of(const PrefillParams& p, int w) {
   const int n_pairs = p.n_heads >> 1;
-  const int e = __ldcg(p.sched + w / n_pairs);
-  const int seq = e >> 16, m = e & 0xFFFF;
-  if (seq < 0 || seq >= p.n_seqs || m >= p.n_mtiles) return PairItem{-1, 0, 0, 0, 0};
-  const int s0 = __ldcg(p.cu_seqlens + seq);
-  const int L = __ldcg(p.cu_seqlens + seq + 1) - s0;
+  const int4 e = __ldcg(p.sched + w / n_pairs);
+  const int seq = e.x, m = e.y, s0 = e.z, L = e.w;
+  if (seq < 0 || seq >= p.n_seqs || m < 0 || m >= p.n_mtiles) return PairItem{-1, 0, 0, 0, 0};
   if (s0 < 0 || L <= m * 128 || s0 + L > p.total_tokens) return PairItem{-1, 0, 0, 0, 0};
   return PairItem{seq, m, 2 * (w % n_pairs), s0, L};
 }
@@ -763,7 +759,13 @@ __global__ void __launch_bounds__(512, 1)
   uint64_t* item_empty = item_full + C::kItemSlots;
   // exp_turn[q][t]: head t's softmax warp on scheduler q may start its exponentials
   uint64_t* exp_turn = item_empty + C::kItemSlots;
-  uint64_t* epi_ready = exp_turn + 8;  // [2] head t's item is complete: its rows' sums are in l_buf
+  // epi_ready[item parity][t]: head t's item is complete, its rows' sums are in
+  // l_buf.  One barrier per item parity: the softmax warps can finish the next
+  // (one-tile) item before the epilogue has waited for this one, and a single
+  // barrier would then have moved two phases on, which a parity wait cannot tell
+  // from none (they cannot get further ahead: the item after that needs a P.V
+  // that waits for the epilogue to release O).
+  uint64_t* epi_ready = exp_turn + 8;
   // l_buf[item parity][head][row]: two items in flight, so a one-tile item's sums
   // cannot overwrite those the epilogue has yet to read
   float* l_buf = reinterpret_cast<float*>(base + C::kLOff);
@@ -800,7 +802,7 @@ __global__ void __launch_bounds__(512, 1)
       ptx::mbar_init(&item_empty[i], 15);  // the three MMA issuers, eight softmax and four epilogue warps
     }
     for (int i = 0; i < 8; ++i) ptx::mbar_init(&exp_turn[i], 1);
-    for (int t = 0; t < 2; ++t) ptx::mbar_init(&epi_ready[t], 4);
+    for (int t = 0; t < 4; ++t) ptx::mbar_init(&epi_ready[t], 4);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -834,13 +836,16 @@ __global__ void __launch_bounds__(512, 1)
       ptx::prefetch_tmap(&tm_k);
       ptx::prefetch_tmap(&tm_v);
     }
-    const long long n_slots = (long long)p.num_blocks * p.block_size;
     PairItem it{};
     while (ok) {
       const int slot = n_claim % C::kItemSlots;
-      int w = 0;
-      if (lane == 0) w = (int)atomicAdd(p.ticket, 1);
-      w = __shfl_sync(0xffffffffu, w, 0);
+      // The first item of CTA b is item b (the heaviest ones, with no atomic on
+      // the way to the first loads); later ones come from the ticket counter.
+      int w = (int)blockIdx.x;
+      if (n_claim > 0) {
+        if (lane == 0) w = (int)atomicAdd(p.ticket, 1) + (int)gridDim.x;
+        w = __shfl_sync(0xffffffffu, w, 0);
+      }
       if (w >= n_items) w = -1;
       if (w >= 0) {
         it = pair_item_of(p, w);
@@ -877,7 +882,6 @@ __global__ void __launch_bounds__(512, 1)
                         kb * 64, it.h0 + t, it.s0 + it.mtile * 128);
       }
       ++q_it;
-      const bool write_kv = p.slot_mapping != nullptr && (it.h0 % p.group) == 0;
       for (int j = 0; j < n_kv; ++j, ++kv_it) {
         const int st = kv_it % S;
         const uint32_t ph = (kv_it / S) & 1;
@@ -896,34 +900,6 @@ __global__ void __launch_bounds__(512, 1)
           ptx::mbar_arrive_expect_tx(&v_full[st], C::kTileBytes);
           for (int kb = 0; kb < C::kKB; ++kb)
             tma_load_3d(vs + kb * C::kBlockBytes, &tm_v, &v_full[st], kb * 64, kvh, it.s0 + j * 128);
-        }
-        if (write_kv && j == it.mtile) {
-          // The diagonal tile holds exactly this query tile's own tokens: copy the
-          // landed rows into their paged slots (slot = block * block_size + offset).
-          ok = __all_sync(0xffffffffu, wait_or_abort(&k_full[st], ph, abort_flag, p.wait_ns) &&
-                                           wait_or_abort(&v_full[st], ph, abort_flag, p.wait_ns));
-          if (!ok) break;
-          const int tok0 = it.s0 + j * 128, rows = min(128, it.L - j * 128);
-          T* kc = reinterpret_cast<T*>(p.k_cache);
-          T* vc = reinterpret_cast<T*>(p.v_cache);
-          long long sl[4];  // slots of rows lane, lane + 32, lane + 64, lane + 96
-#pragma unroll
-          for (int q = 0; q < 4; ++q) sl[q] = lane + 32 * q < rows ? __ldcg(p.slot_mapping + tok0 + lane + 32 * q) : -1;
-          for (int i0 = 0; i0 < rows * (D / 8); i0 += 32) {
-            const int i = i0 + lane;
-            const int r = min(i / (D / 8), 127), c8 = i % (D / 8);
-            long long slot = -1;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const long long v = __shfl_sync(0xffffffffu, sl[q], r & 31);
-              slot = (r >> 5) == q ? v : slot;
-            }
-            if (i >= rows * (D / 8) || slot < 0 || slot >= n_slots) continue;
-            const uint32_t off = (c8 / 8) * C::kBlockBytes + r * 128 + ((((c8 & 7) ^ (r & 7))) << 4);
-            const size_t dst = ((size_t)slot * p.n_kv_heads + kvh) * D + c8 * 8;
-            *reinterpret_cast<uint4*>(kc + dst) = *reinterpret_cast<const uint4*>(ks + off);
-            *reinterpret_cast<uint4*>(vc + dst) = *reinterpret_cast<const uint4*>(vs + off);
-          }
         }
       }
     }
@@ -1047,8 +1023,35 @@ __global__ void __launch_bounds__(512, 1)
       if (got == 0) break;
       g += pair_kv_tiles(p, it);  // g - 1: the item's last key tile
       const int q_pos = it.mtile * 128 + r;
+      if (p.slot_mapping != nullptr && it.h0 % p.group == 0 && q_pos < it.L) {
+        // Paged K/V write (the first pair of every KV head's group): row q_pos of
+        // this prompt's k and v goes to its slot (block * block_size + offset).  The
+        // rows were just TMA-loaded for this item, so they come from L2; the copy
+        // overlaps the item's softmax instead of holding up the producer's loads.
+        const long long slot = __ldcg(p.slot_mapping + it.s0 + q_pos);
+        const long long n_slots = (long long)p.num_blocks * p.block_size;
+        if (slot >= 0 && slot < n_slots) {
+          const int kvh = it.h0 / p.group;
+          const size_t src = ((size_t)(it.s0 + q_pos) * p.n_kv_heads + kvh) * D;
+          const size_t dst = ((size_t)slot * p.n_kv_heads + kvh) * D;
+#pragma unroll
+          for (int kv = 0; kv < 2; ++kv) {
+            const uint4* sp = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(kv ? p.v : p.k) + src);
+            uint4* dp = reinterpret_cast<uint4*>(reinterpret_cast<T*>(kv ? p.v_cache : p.k_cache) + dst);
+#pragma unroll
+            for (int c0 = 0; c0 < D / 8; c0 += 4) {
+              uint4 x[4];
+#pragma unroll
+              for (int c = 0; c < 4; ++c) x[c] = __ldcg(sp + c0 + c);
+#pragma unroll
+              for (int c = 0; c < 4; ++c) dp[c0 + c] = x[c];
+            }
+          }
+        }
+      }
       for (int t = 0; t < 2 && ok; ++t) {
-        ok = __all_sync(0xffffffffu, wait_or_abort(&epi_ready[t], item_it & 1, abort_flag, p.wait_ns) &&
+        ok = __all_sync(0xffffffffu, wait_or_abort(&epi_ready[(item_it & 1) * 2 + t], (item_it >> 1) & 1, abort_flag,
+                                                   p.wait_ns) &&
                                          wait_or_abort(&pv_done[t], (g - 1) & 1, abort_flag, p.wait_ns));
         if (!ok) break;
         umma::fence_after_sync();
@@ -1199,7 +1202,7 @@ __global__ void __launch_bounds__(512, 1)
       // finished before that item's first P.V (and so our previous P store) ran.
       l_buf[((item_it & 1) * 2 + t) * 128 + r] = l0 + l1;
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&epi_ready[t]);
+      if (lane == 0) ptx::mbar_arrive(&epi_ready[(item_it & 1) * 2 + t]);
       ++item_it;
     }
     if (!ok) report(p.status);
@@ -1312,7 +1315,7 @@ __global__ void __launch_bounds__(128) flash_prefill_simt_kernel(const PrefillPa
 constexpr int kMaxBands = 4096;  // query tiles per prompt: max_seqlen <= 524288
 
 __global__ void __launch_bounds__(1024) prefill_schedule_kernel(const int32_t* __restrict__ cu, int n_seqs,
-                                                                int n_bands, int capacity, int32_t* sched,
+                                                                int n_bands, int capacity, int4* sched,
                                                                 int32_t* count, int* ticket, int* status) {
   __shared__ int band[kMaxBands];
   // let the attention kernel start its prologue now; it waits for this grid
@@ -1338,10 +1341,11 @@ __global__ void __launch_bounds__(1024) prefill_schedule_kernel(const int32_t* _
   }
   __syncthreads();
   for (int s = threadIdx.x; s < n_seqs; s += blockDim.x) {
-    const int nt = min((cu[s + 1] - cu[s] + 127) / 128, n_bands);
+    const int s0 = cu[s], L = cu[s + 1] - s0;
+    const int nt = min((L + 127) / 128, n_bands);
     for (int m = nt - 1; m >= 0; --m) {
       const int pos = atomicAdd(&band[m], 1);
-      if (pos < capacity) sched[pos] = (s << 16) | m;
+      if (pos < capacity) sched[pos] = make_int4(s, m, s0, L);
     }
   }
 }
@@ -1379,7 +1383,7 @@ int launch_tc(const PrefillParams& p, int total, int sched_capacity, CUtensorMap
   if (rc != TVK_OK) return rc;
   auto kern = flash_prefill_tc_kernel<T, D>;
   prefill_schedule_kernel<<<1, 1024, 0, stream>>>(p.cu_seqlens, p.n_seqs, p.n_mtiles, sched_capacity,
-                                                  const_cast<int32_t*>(p.sched), const_cast<int32_t*>(p.sched_count),
+                                                  const_cast<int4*>(p.sched), const_cast<int32_t*>(p.sched_count),
                                                   p.ticket, p.status);
   TVK_CHECK_LAUNCH("prefill_schedule");
   static unsigned long long attr_mask = 0;
@@ -1443,7 +1447,7 @@ int launch_pair(const PrefillParams& p, int total, int sched_capacity, CUtensorM
     attr_mask |= 1ull << dev;
   }
   prefill_schedule_kernel<<<1, 1024, 0, stream>>>(p.cu_seqlens, p.n_seqs, p.n_mtiles, sched_capacity,
-                                                  const_cast<int32_t*>(p.sched), const_cast<int32_t*>(p.sched_count),
+                                                  const_cast<int4*>(p.sched), const_cast<int32_t*>(p.sched_count),
                                                   p.ticket, p.status);
   TVK_CHECK_LAUNCH("prefill_schedule");
   const long long items = (long long)p.n_mtiles * p.n_seqs * (p.n_heads / 2);
@@ -1496,7 +1500,7 @@ extern "C" int tvk_prefill_select_kernel(int choice) {
 extern "C" size_t tvk_flash_prefill_workspace_size(int n_seqs, int total_tokens) {
   if (n_seqs < 0 || total_tokens < 0) return tvk::kWorkspaceHeader;
   const size_t items = (size_t)total_tokens / 128 + (size_t)n_seqs + 1;
-  return tvk::kWorkspaceHeader + ((items * 4 + 255) / 256) * 256;
+  return tvk::kWorkspaceHeader + ((items * sizeof(int4) + 255) / 256) * 256;
 }
 
 extern "C" int tvk_flash_prefill_attention(const void* q, const void* k, const void* v, void* out,
@@ -1564,8 +1568,8 @@ extern "C" int tvk_flash_prefill_attention(const void* q, const void* k, const v
     int32_t* w32 = reinterpret_cast<int32_t*>(workspace);
     p.sched_count = w32 + 1;
     p.ticket = w32 + 2;
-    p.sched = w32 + tvk::kWorkspaceHeader / 4;
-    const int cap = (int)((need - tvk::kWorkspaceHeader) / 4);
+    p.sched = reinterpret_cast<const int4*>(reinterpret_cast<uint8_t*>(workspace) + tvk::kWorkspaceHeader);
+    const int cap = (int)((need - tvk::kWorkspaceHeader) / sizeof(int4));
     p.sched_cap = cap;
     // Heads in pairs sharing a KV head: the paired kernel (one CTA per SM, both heads'
     // softmax in flight); otherwise (one query head per KV head, or an odd group) the

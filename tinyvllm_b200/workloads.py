@@ -92,11 +92,15 @@ def decode_config1(device="cuda") -> DecodeCase:
 
 
 def decode_config3(device="cuda", batch: int = 256, dtype=torch.float16, ctx_lo: int = 128,
-                   ctx_hi: int = 4096, seed_offset: int = 0) -> DecodeCase:
+                   ctx_hi: int = 4096, seed_offset: int = 0, shared_contexts: bool = False) -> DecodeCase:
+    """Config 3's decode batch.  ``seed_offset`` reseeds the values and the tables;
+    with ``shared_contexts`` the context lengths stay those of offset 0, so that
+    every rank of a weak-scaling run holds the same amount of K/V."""
     rng = np.random.default_rng(SEED_BASE + 3 + seed_offset)
     gen = torch.Generator(device=device).manual_seed(SEED_BASE + 3 + seed_offset)
     Hq, Hkv, D, bs = 32, 8, 128, 16
-    ctx = rng.integers(ctx_lo, ctx_hi + 1, size=batch).astype(np.int32)
+    ctx_rng = np.random.default_rng(SEED_BASE + 3) if (shared_contexts and seed_offset) else rng
+    ctx = ctx_rng.integers(ctx_lo, ctx_hi + 1, size=batch).astype(np.int32)
     need = (ctx + bs - 1) // bs
     N = int(math.ceil(1.2 * int(need.sum())))
     bt = _tables_from_pool(rng, N, ctx, bs)
