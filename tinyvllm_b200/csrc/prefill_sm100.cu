@@ -657,6 +657,7 @@ struct PairItem {
 
 __device__ __forceinline__ PairItem pair_item_of(const PrefillParams& p, int w) {
   const int n_pairs = p.n_heads >> 1;
+  if (w < 0 || w / n_pairs >= p.sched_cap) return PairItem{-1, 0, 0, 0, 0};
   const int4 e = __ldcg(p.sched + w / n_pairs);
   const int seq = e.x, m = e.y, s0 = e.z, L = e.w;
   if (seq < 0 || seq >= p.n_seqs || m < 0 || m >= p.n_mtiles) return PairItem{-1, 0, 0, 0, 0};
@@ -846,9 +847,12 @@ __global__ void __launch_bounds__(512, 1)
         if (lane == 0) w = (int)atomicAdd(p.ticket, 1) + (int)gridDim.x;
         w = __shfl_sync(0xffffffffu, w, 0);
       }
+      // The entry is read before it is checked against the list length, so that the
+      // two reads overlap; an entry at or past the length is discarded.
+      const PairItem cand = pair_item_of(p, w);
       if (w >= n_items) w = -1;
       if (w >= 0) {
-        it = pair_item_of(p, w);
+        it = cand;
         if (it.seq < 0) {  // a corrupt schedule entry: stop here and say so
           report(p.status);
           w = -1;
