@@ -229,6 +229,38 @@ def test_many_prompts_take_the_device_schedule(cuda, kernel, n):
     assert workspace_status(kind="prefill") == 0
 
 
+@pytest.mark.parametrize("n,hi,max_extra", [(32, 700, 0), (9, 260, 3000), (1, 5, 0)])
+def test_small_batches_with_shared_tile_counts(cuda, kernel, n, hi, max_extra):
+    """Up to 32 prompts, many with the same number of query tiles, and a
+    ``max_seqlen`` that may exceed the longest prompt (empty top bands of the
+    schedule): every prompt's rows and its paged K/V write come out exactly once,
+    on two calls in a row (CTA b's first item is item b, the rest come from the
+    ticket counter)."""
+    from tinyvllm_b200.attention import flash_prefill_attention_varlen, workspace_status
+    rng = np.random.default_rng(700 + n)
+    lens = [int(x) for x in rng.integers(1, hi, size=n)]
+    q, k, v, cu, _ = _config2_inputs(cuda, torch.float16, lens=lens)
+    T = sum(lens)
+    n_blocks = sum((L + 15) // 16 for L in lens) + 3
+    slots = torch.from_numpy(rng.permutation(n_blocks * 16)[:T].astype(np.int64)).to(cuda)
+    kc = torch.zeros(n_blocks, 16, 4, 64, dtype=torch.float16, device=cuda)
+    vc = torch.zeros_like(kc)
+    for _ in range(2):
+        out = flash_prefill_attention_varlen(q, k, v, cu, max(lens) + max_extra, True, slot_mapping=slots,
+                                             k_cache=kc, v_cache=vc, check=True)
+        torch.cuda.synchronize()
+        for i in range(n):
+            a, b = int(cu[i]), int(cu[i + 1])
+            _check(out[a:b], _oracle(q[a:b], k[a:b], v[a:b]), torch.float16)
+        exp_k = torch.zeros(n_blocks * 16, 4, 64, dtype=torch.float16, device=cuda)
+        exp_v = torch.zeros_like(exp_k)
+        exp_k[slots] = k
+        exp_v[slots] = v
+        assert torch.equal(kc.view(-1, 4, 64), exp_k)
+        assert torch.equal(vc.view(-1, 4, 64), exp_v)
+    assert workspace_status(kind="prefill") == 0
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("L,nh,nkv,D", [(300, 32, 4, 64), (129, 8, 2, 64), (260, 32, 8, 128), (1, 16, 4, 64)])
 def test_non_causal_gqa(cuda, kernel, dtype, L, nh, nkv, D):
