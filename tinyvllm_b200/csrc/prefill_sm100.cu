@@ -626,8 +626,9 @@ struct PairCfg {
   static constexpr int kBarOff = kVOff + kStages * kTileBytes;
   static constexpr int kItemSlots = 4;
   // q_full[QB], q_empty[QB], k_full[S], v_full[S], k_empty[S], v_empty[S], s_full[2], s_free[2], p_full[2],
-  // pv_done[2], o_empty[2], final[3], item_full[4], item_empty[4], exp_turn[4][2], epi_ready[2][2]
-  static constexpr int kNumBars = 2 * kQBufs + 4 * kStages + 10 + 3 + 2 * kItemSlots + 8 + 4;
+  // pv_done[2], o_empty[2], final[3], item_full[4], item_empty[4], exp_turn[4][2], epi_ready[2][2],
+  // item_started
+  static constexpr int kNumBars = 2 * kQBufs + 4 * kStages + 10 + 3 + 2 * kItemSlots + 8 + 4 + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kLOff = kMiscOff + 16 + 32 * kItemSlots;  // row sums for the epilogue [2][2][128]
   static constexpr int kUsed = kLOff + 2 * 2 * 128 * 4;
@@ -767,6 +768,11 @@ __global__ void __launch_bounds__(512, 1)
   // from none (they cannot get further ahead: the item after that needs a P.V
   // that waits for the epilogue to release O).
   uint64_t* epi_ready = exp_turn + 8;
+  // The S issuer has taken item n.  The producer claims item n + 1 only then: a CTA
+  // holds at most the running item and the next, so the last, small items of the
+  // list go to CTAs that are about to run out of work instead of queueing behind
+  // two items on one CTA.
+  uint64_t* item_started = epi_ready + 4;
   // l_buf[item parity][head][row]: two items in flight, so a one-tile item's sums
   // cannot overwrite those the epilogue has yet to read
   float* l_buf = reinterpret_cast<float*>(base + C::kLOff);
@@ -804,6 +810,7 @@ __global__ void __launch_bounds__(512, 1)
     }
     for (int i = 0; i < 8; ++i) ptx::mbar_init(&exp_turn[i], 1);
     for (int t = 0; t < 4; ++t) ptx::mbar_init(&epi_ready[t], 4);
+    ptx::mbar_init(item_started, 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -844,6 +851,10 @@ __global__ void __launch_bounds__(512, 1)
       // the way to the first loads); later ones come from the ticket counter.
       int w = (int)blockIdx.x;
       if (n_claim > 0) {
+        // Item n_claim - 1 has been taken by the S issuer (it has taken every item
+        // before it, so the barrier's phase cannot be two behind this wait).
+        ok = __all_sync(0xffffffffu, wait_or_abort(item_started, (n_claim - 1) & 1, abort_flag, p.wait_ns));
+        if (!ok) break;
         if (lane == 0) w = (int)atomicAdd(p.ticket, 1) + (int)gridDim.x;
         w = __shfl_sync(0xffffffffu, w, 0);
       }
@@ -930,6 +941,7 @@ __global__ void __launch_bounds__(512, 1)
           ok = got == 0;
           break;
         }
+        ptx::mbar_arrive(item_started);  // the producer may claim the next item
         const int n_kv = pair_kv_tiles(p, it);
         const int qb = q_it % QB;
         ok = wait_or_abort(&q_full[qb], (q_it / QB) & 1, abort_flag, p.wait_ns);
