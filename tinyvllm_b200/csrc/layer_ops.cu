@@ -18,6 +18,12 @@
 
 namespace {
 
+// Every kernel here is launched as a programmatic dependent (tvk::launch_pdl):
+// it waits for the kernel before it, and its memory, before its first read, then
+// lets the next launch on the stream start.
+#define TVK_PDL_ENTER() asm volatile("griddepcontrol.wait;\n\tgriddepcontrol.launch_dependents;" ::: "memory")
+
+
 // ---- vector helpers: 8 elements of a 16-bit type or 4 floats per 16 bytes ----
 template <typename T> struct Vec { static constexpr int N = 16 / sizeof(T); };
 
@@ -78,6 +84,7 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_kernel(const T* __restr
                                                                 T* residual_out, const T* __restrict__ w,
                                                                 T* __restrict__ out, int dim, float eps,
                                                                 KvAppend<T> kv) {
+  TVK_PDL_ENTER();
   constexpr int N = Vec<T>::N;
   __shared__ float red[32];
   const size_t row = blockIdx.x;
@@ -158,6 +165,7 @@ template <typename T>
 __global__ void rope_kernel(T* q, T* k, const T* v, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
                             const int32_t* __restrict__ pos, int n_tokens, int hq, int hkv, int D, int max_pos,
                             const int64_t* __restrict__ slots, T* k_cache, T* v_cache, long long n_slots) {
+  TVK_PDL_ENTER();
   constexpr int N = Vec<T>::N;
   const int vpr = D / N;  // vectors per head row
   const long long total = (long long)n_tokens * (hq + hkv) * vpr;
@@ -204,6 +212,7 @@ __global__ void qkv_rope_kernel(const T* __restrict__ qkv, long long row_stride,
                                 const float* __restrict__ sin_t, const int32_t* __restrict__ pos, int n_tokens, int hq,
                                 int hkv, int D, int max_pos, const int64_t* __restrict__ slots, T* k_cache,
                                 T* v_cache, long long n_slots) {
+  TVK_PDL_ENTER();
   constexpr int N = Vec<T>::N;
   const int vpr = D / N;
   const int heads = hq + 2 * hkv;
@@ -252,6 +261,7 @@ __global__ void qkv_rope_kernel(const T* __restrict__ qkv, long long row_stride,
 template <typename T>
 __global__ void write_kv_kernel(const T* __restrict__ k, const T* __restrict__ v, const int64_t* __restrict__ slots,
                                 T* k_cache, T* v_cache, int n_tokens, int row_elems, long long n_slots) {
+  TVK_PDL_ENTER();
   constexpr int N = Vec<T>::N;
   const int vpr = row_elems / N;
   const long long total = (long long)n_tokens * vpr;
@@ -272,6 +282,7 @@ __global__ void write_kv_kernel(const T* __restrict__ k, const T* __restrict__ v
 template <typename T>
 __global__ void silu_mul_kernel(const T* __restrict__ a, const T* __restrict__ b, T* __restrict__ out, int rows,
                                 int cols, long long a_stride, long long b_stride, long long o_stride) {
+  TVK_PDL_ENTER();
   constexpr int N = Vec<T>::N;
   const int vpr = cols / N;
   const long long total = (long long)rows * vpr;
@@ -298,6 +309,7 @@ __global__ void silu_mul_kernel(const T* __restrict__ a, const T* __restrict__ b
 template <typename T>
 __global__ void embedding_kernel(const T* __restrict__ table, const int32_t* __restrict__ tokens, T* __restrict__ out,
                                  int n_tokens, int dim, int vocab, int* status) {
+  TVK_PDL_ENTER();
   constexpr int N = Vec<T>::N;
   const int vpr = dim / N;
   const long long total = (long long)n_tokens * vpr;
@@ -329,6 +341,7 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
 template <typename T>
 __global__ void __launch_bounds__(kArgmaxThreads) argmax_kernel(const T* __restrict__ logits, int32_t* __restrict__ out,
                                                                 int vocab, long long row_stride, int vec) {
+  TVK_PDL_ENTER();
   constexpr int N = Vec<T>::N;
   __shared__ float sv[32];
   __shared__ int si[32];
@@ -448,6 +461,7 @@ template <typename T>
 __global__ void __launch_bounds__(kArgmaxThreads) argmax16_kernel(const T* __restrict__ logits,
                                                                   int32_t* __restrict__ out, int vocab,
                                                                   long long row_stride) {
+  TVK_PDL_ENTER();
   using T2 = typename Pack2<T>::type;
   __shared__ float sv[32];
   __shared__ int si[32];
@@ -552,10 +566,10 @@ template <typename T>
 void launch_rms_norm(int rows, int dim, cudaStream_t s, const T* x, const T* residual, T* residual_out, const T* w,
                      T* out, float eps, const KvAppend<T>& kv) {
   const int vpt = (dim / Vec<T>::N + kNormThreads - 1) / kNormThreads;
-  if (vpt <= 1) rms_norm_kernel<T, 1><<<rows, kNormThreads, 0, s>>>(x, residual, residual_out, w, out, dim, eps, kv);
-  else if (vpt <= 2) rms_norm_kernel<T, 2><<<rows, kNormThreads, 0, s>>>(x, residual, residual_out, w, out, dim, eps, kv);
-  else if (vpt <= 4) rms_norm_kernel<T, 4><<<rows, kNormThreads, 0, s>>>(x, residual, residual_out, w, out, dim, eps, kv);
-  else rms_norm_kernel<T, kNormMaxVec><<<rows, kNormThreads, 0, s>>>(x, residual, residual_out, w, out, dim, eps, kv);
+  if (vpt <= 1) tvk::launch_pdl(rms_norm_kernel<T, 1>, rows, kNormThreads, 0, s, x, residual, residual_out, w, out, dim, eps, kv);
+  else if (vpt <= 2) tvk::launch_pdl(rms_norm_kernel<T, 2>, rows, kNormThreads, 0, s, x, residual, residual_out, w, out, dim, eps, kv);
+  else if (vpt <= 4) tvk::launch_pdl(rms_norm_kernel<T, 4>, rows, kNormThreads, 0, s, x, residual, residual_out, w, out, dim, eps, kv);
+  else tvk::launch_pdl(rms_norm_kernel<T, kNormMaxVec>, rows, kNormThreads, 0, s, x, residual, residual_out, w, out, dim, eps, kv);
 }
 
 }  // namespace
@@ -617,7 +631,7 @@ extern "C" int tvk_rope(void* q, void* k, const float* cos_table, const float* s
   TVK_CHECK_ARG(aligned16(q) && aligned16(k), "q and k must be 16-byte aligned");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const long long work = (long long)n_tokens * (n_heads + n_kv_heads) * (head_dim / vec_elems(dtype));
-  TVK_DISPATCH(dtype, rope_kernel<T><<<grid_for(work, 256), 256, 0, s>>>(
+  TVK_DISPATCH(dtype, tvk::launch_pdl(rope_kernel<T>, grid_for(work, 256), 256, 0, s, 
       (T*)q, (T*)k, nullptr, cos_table, sin_table, positions, n_tokens, n_heads, n_kv_heads, head_dim, max_pos,
       nullptr, nullptr, nullptr, 0));
   TVK_CHECK_LAUNCH("rope");
@@ -638,7 +652,7 @@ extern "C" int tvk_rope_write_kv(void* q, void* k, const void* v, const float* c
                 "pointers must be 16-byte aligned");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const long long work = (long long)n_tokens * (n_heads + n_kv_heads) * (head_dim / vec_elems(dtype));
-  TVK_DISPATCH(dtype, rope_kernel<T><<<grid_for(work, 256), 256, 0, s>>>(
+  TVK_DISPATCH(dtype, tvk::launch_pdl(rope_kernel<T>, grid_for(work, 256), 256, 0, s, 
       (T*)q, (T*)k, (const T*)v, cos_table, sin_table, positions, n_tokens, n_heads, n_kv_heads, head_dim, max_pos,
       slots, (T*)k_cache, (T*)v_cache, (long long)num_blocks * block_size));
   TVK_CHECK_LAUNCH("rope_write_kv");
@@ -664,7 +678,7 @@ extern "C" int tvk_qkv_rope(const void* qkv, long long row_stride, void* q, void
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const long long work = (long long)n_tokens * (n_heads + 2 * n_kv_heads) * (head_dim / N);
-  TVK_DISPATCH(dtype, qkv_rope_kernel<T><<<grid_for(work, 256), 256, 0, s>>>(
+  TVK_DISPATCH(dtype, tvk::launch_pdl(qkv_rope_kernel<T>, grid_for(work, 256), 256, 0, s, 
       (const T*)qkv, row_stride, (T*)q, (T*)k, (T*)v, cos_table, sin_table, positions, n_tokens, n_heads, n_kv_heads,
       head_dim, max_pos, slots, (T*)k_cache, (T*)v_cache, slots ? (long long)num_blocks * block_size : 0));
   TVK_CHECK_LAUNCH("qkv_rope");
@@ -683,7 +697,7 @@ extern "C" int tvk_write_kv_slots(const void* k, const void* v, const int64_t* s
                 "pointers must be 16-byte aligned");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const long long work = (long long)n_tokens * (row / vec_elems(dtype));
-  TVK_DISPATCH(dtype, write_kv_kernel<T><<<grid_for(work, 256), 256, 0, s>>>(
+  TVK_DISPATCH(dtype, tvk::launch_pdl(write_kv_kernel<T>, grid_for(work, 256), 256, 0, s, 
       (const T*)k, (const T*)v, slots, (T*)k_cache, (T*)v_cache, n_tokens, row, (long long)num_blocks * block_size));
   TVK_CHECK_LAUNCH("write_kv");
   return TVK_OK;
@@ -700,7 +714,7 @@ extern "C" int tvk_silu_mul(const void* a, const void* b, void* out, int rows, i
   TVK_CHECK_ARG(aligned16(a) && aligned16(b) && aligned16(out), "pointers must be 16-byte aligned");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const long long work = (long long)rows * (cols / N);
-  TVK_DISPATCH(dtype, silu_mul_kernel<T><<<grid_for(work, 256), 256, 0, s>>>(
+  TVK_DISPATCH(dtype, tvk::launch_pdl(silu_mul_kernel<T>, grid_for(work, 256), 256, 0, s, 
       (const T*)a, (const T*)b, (T*)out, rows, cols, a_stride, b_stride, out_stride));
   TVK_CHECK_LAUNCH("silu_mul");
   return TVK_OK;
@@ -715,7 +729,7 @@ extern "C" int tvk_embedding(const void* table, const int32_t* tokens, void* out
   TVK_CHECK_ARG(aligned16(table) && aligned16(out), "pointers must be 16-byte aligned");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const long long work = (long long)n_tokens * (dim / vec_elems(dtype));
-  TVK_DISPATCH(dtype, embedding_kernel<T><<<grid_for(work, 256), 256, 0, s>>>(
+  TVK_DISPATCH(dtype, tvk::launch_pdl(embedding_kernel<T>, grid_for(work, 256), 256, 0, s, 
       (const T*)table, tokens, (T*)out, n_tokens, dim, vocab, status));
   TVK_CHECK_LAUNCH("embedding");
   return TVK_OK;
@@ -729,13 +743,13 @@ extern "C" int tvk_argmax(const void* logits, int32_t* out, int rows, int vocab,
   const int vec = aligned16(logits) && row_stride % vec_elems(dtype) == 0;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (vec && dtype == TVK_DTYPE_F16) {
-    argmax16_kernel<__half><<<rows, kArgmaxThreads, 0, s>>>((const __half*)logits, out, vocab, row_stride);
+    tvk::launch_pdl(argmax16_kernel<__half>, rows, kArgmaxThreads, 0, s, (const __half*)logits, out, vocab, row_stride);
   } else if (vec && dtype == TVK_DTYPE_BF16) {
-    argmax16_kernel<__nv_bfloat16><<<rows, kArgmaxThreads, 0, s>>>((const __nv_bfloat16*)logits, out, vocab,
+    tvk::launch_pdl(argmax16_kernel<__nv_bfloat16>, rows, kArgmaxThreads, 0, s, (const __nv_bfloat16*)logits, out, vocab,
                                                                     row_stride);
   } else {
     TVK_DISPATCH(dtype,
-                 argmax_kernel<T><<<rows, kArgmaxThreads, 0, s>>>((const T*)logits, out, vocab, row_stride, vec));
+                 tvk::launch_pdl(argmax_kernel<T>, rows, kArgmaxThreads, 0, s, (const T*)logits, out, vocab, row_stride, vec));
   }
   TVK_CHECK_LAUNCH("argmax");
   return TVK_OK;

@@ -204,6 +204,9 @@ __global__ void __launch_bounds__(160, 2)
     ptx::fence_mbar_init();
   }
   __syncthreads();
+  // Launched as a programmatic dependent: wait for the kernel before it (which
+  // may have written q, the tables or this step's K/V) before any global read.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (warp == 4) {
     // ---------------- producer warp ----------------------------------------
@@ -624,6 +627,7 @@ __device__ __forceinline__ void load4(const T* src, float* dst) {
 
 template <typename T, int D>
 __global__ void __launch_bounds__(128) paged_decode_simt_kernel(const DecodeParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // programmatic dependent launch
   constexpr int DP = D + 4;               // padded row (floats)
   constexpr int MAXK = kMaxGroup * D / 128;  // (head, dim) outputs per thread
   __shared__ __align__(16) float qs[kMaxGroup][D];
@@ -769,6 +773,7 @@ __global__ void __launch_bounds__(128) paged_decode_simt_kernel(const DecodePara
 // flight per lane.
 template <typename T, int D>
 __global__ void __launch_bounds__(128) paged_decode_combine_kernel(const DecodeParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // programmatic dependent launch
   const int kvh = blockIdx.x, b = blockIdx.y;
   const int ctx = effective_ctx(p, b);
   if (ctx <= 0) return;
@@ -923,7 +928,7 @@ int launch_tc(const DecodeParams& p, const void* k_cache, const void* v_cache, C
   const long long slots = (long long)num_sms[dev] * ctas_per_sm[dev][p.group];
   // Persistent grids fill the resident slots; otherwise one CTA per unit.
   const int grid = (int)(p.dynamic && units > slots ? slots : units);
-  kern<<<grid, 160, smem, stream>>>(p, tmk, tmv);
+  TVK_CHECK_CUDA(tvk::launch_pdl(kern, grid, 160, smem, stream, p, tmk, tmv));
   TVK_CHECK_LAUNCH("paged_decode_tc");
   return TVK_OK;
 }
@@ -942,9 +947,9 @@ int launch_typed(DecodeParams& p, bool use_tc, CUtensorMapDataType tdt, cudaStre
   } else {
     dim3 grid(p.max_splits, p.n_kv_heads, p.batch);
     switch (p.head_dim) {
-      case 32: paged_decode_simt_kernel<T, 32><<<grid, 128, 0, stream>>>(p); break;
-      case 64: paged_decode_simt_kernel<T, 64><<<grid, 128, 0, stream>>>(p); break;
-      default: paged_decode_simt_kernel<T, 128><<<grid, 128, 0, stream>>>(p); break;
+      case 32: tvk::launch_pdl(paged_decode_simt_kernel<T, 32>, grid, 128, 0, stream, p); break;
+      case 64: tvk::launch_pdl(paged_decode_simt_kernel<T, 64>, grid, 128, 0, stream, p); break;
+      default: tvk::launch_pdl(paged_decode_simt_kernel<T, 128>, grid, 128, 0, stream, p); break;
     }
     TVK_CHECK_LAUNCH("paged_decode_simt");
   }
@@ -952,9 +957,9 @@ int launch_typed(DecodeParams& p, bool use_tc, CUtensorMapDataType tdt, cudaStre
   if (p.max_splits > 1) {
     const dim3 cgrid(p.n_kv_heads, p.batch);
     switch (p.head_dim) {
-      case 32: paged_decode_combine_kernel<T, 32><<<cgrid, 128, 0, stream>>>(p); break;
-      case 64: paged_decode_combine_kernel<T, 64><<<cgrid, 128, 0, stream>>>(p); break;
-      default: paged_decode_combine_kernel<T, 128><<<cgrid, 128, 0, stream>>>(p); break;
+      case 32: tvk::launch_pdl(paged_decode_combine_kernel<T, 32>, cgrid, 128, 0, stream, p); break;
+      case 64: tvk::launch_pdl(paged_decode_combine_kernel<T, 64>, cgrid, 128, 0, stream, p); break;
+      default: tvk::launch_pdl(paged_decode_combine_kernel<T, 128>, cgrid, 128, 0, stream, p); break;
     }
     TVK_CHECK_LAUNCH("paged_decode_combine");
   }

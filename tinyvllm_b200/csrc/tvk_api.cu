@@ -1,6 +1,7 @@
 // tvk_api.cu -- library-wide C ABI pieces: version, thread-local last error,
 // and the driver entry point for TMA tensor-map encoding.
 #include <stdarg.h>
+#include <stdlib.h>
 #include <mutex>
 
 #include "tvk_common.cuh"
@@ -27,6 +28,14 @@ EncodeTiledFn encode_tiled_fn() {
       fn = reinterpret_cast<EncodeTiledFn>(p);
   });
   return fn;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("TVK_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 static thread_local WaitTest g_wait_test = {false, 0};

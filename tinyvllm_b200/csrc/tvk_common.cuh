@@ -69,6 +69,29 @@ struct WaitTest {
 };
 WaitTest take_wait_test();
 
+// Programmatic dependent launch of the layer and decode kernels (their launch
+// overlaps the tail of the kernel before them; each waits for it with
+// griddepcontrol.wait before its first read of global memory).  On unless the
+// environment sets TVK_PDL=0.
+bool pdl_enabled();
+
+// Launch `kern` with the programmatic-serialization attribute when enabled.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
+}
+
 }  // namespace tvk
 
 // ----------------------------------------------------------------------------
