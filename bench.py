@@ -735,6 +735,8 @@ def engine4_line(args, rank: int, world: int, local_rank: int):
     steps = args.engine_steps
     ctx_trace = []
 
+    step_wall = {"prefill": [], "decode": []}   # host wall time of each engine step, by kind
+
     def one_run(trace=False):
         i, made = 0, 0
         while i < len(prompts) or eng.has_unfinished():
@@ -744,7 +746,11 @@ def engine4_line(args, rank: int, world: int, local_rank: int):
                     i += 1
             if trace:
                 ctx_trace.append([s.get_len() for s in eng.scheduler.running.values()])
+            p0 = eng.stats["prefill_tokens"]
+            t = time.perf_counter()
             made += sum(len(o.tokens) for o in eng.step())
+            if not trace:
+                step_wall["prefill" if eng.stats["prefill_tokens"] != p0 else "decode"].append(time.perf_counter() - t)
         return made
 
     one_run(trace=True)        # warm-up (graph captures) and the per-step context trace
@@ -790,6 +796,9 @@ def engine4_line(args, rank: int, world: int, local_rank: int):
                      "note": "(weights once per engine step + live K/V each decode step reads) / run time; "
                              "prefill FLOPs are not counted, so this is a lower bound on the HBM share"},
         "wall_ms_per_step": dt * 1e3 / steps,
+        "engine_step_wall_ms": {k: {"count": len(v) // steps, "mean": 1e3 * statistics.mean(v) if v else None,
+                                    "total_per_run": 1e3 * sum(v) / steps}
+                                for k, v in step_wall.items()},
         "clocks": clk, "cpu_baseline": cpu,
         "gpu_launches": None,
         "note": "device events around whole engine runs, host scheduling included (every engine step "
