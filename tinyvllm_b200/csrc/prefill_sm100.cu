@@ -1042,8 +1042,8 @@ __global__ void __launch_bounds__(512, 1)
       if (p.slot_mapping != nullptr && it.h0 % p.group == 0 && q_pos < it.L) {
         // Paged K/V write (the first pair of every KV head's group): row q_pos of
         // this prompt's k and v goes to its slot (block * block_size + offset).  The
-        // rows were just TMA-loaded for this item, so they come from L2; the copy
-        // overlaps the item's softmax instead of holding up the producer's loads.
+        // producer loads the same rows for this item, so they are usually in L2; the
+        // copy overlaps the item's softmax instead of holding up the producer's loads.
         const long long slot = __ldcg(p.slot_mapping + it.s0 + q_pos);
         const long long n_slots = (long long)p.num_blocks * p.block_size;
         if (slot >= 0 && slot < n_slots) {
