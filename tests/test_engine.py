@@ -233,3 +233,47 @@ def test_out_of_blocks_raises_the_reference_error(cuda):
     eng.add_request(list(range(40)), SamplingParams(max_tokens=2))
     with pytest.raises(RuntimeError, match="Out of KV cache memory!"):
         eng.step()
+
+
+@pytest.mark.parametrize("dtype", ["float32", "float16"])
+def test_prefill_graph_matches_eager_prefill(cuda, dtype):
+    """A prefill replayed as a CUDA graph over a padded token buffer samples the same
+    first tokens as the eager ragged prefill and writes the same K/V into the same
+    slots; the padding prompt and the capture-time runs write nothing."""
+    from tinyvllm_b200 import layers
+    from tinyvllm_b200.model import KVCache
+    model = _tiny(dtype, 256, 4, 2, seed=5)
+    c = model.config
+    rng = np.random.default_rng(9)
+    lens = [37, 1, 130]
+    toks = rng.integers(0, c.vocab_size, size=sum(lens)).astype(np.int32)
+    pos = np.concatenate([np.arange(L, dtype=np.int32) for L in lens])
+    nb = 64
+    perm = rng.permutation(nb)[:sum(-(-L // 16) for L in lens)]
+    slots, b = [], 0
+    for L in lens:
+        blocks = perm[b:b + -(-L // 16)]
+        b += len(blocks)
+        slots.extend(int(blocks[t // 16]) * 16 + t % 16 for t in range(L))
+    slots = np.asarray(slots, dtype=np.int64)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    kv_e = KVCache(c.n_layers, nb, 16, c.n_kv_heads, c.head_dim, c.torch_dtype, cuda)
+    logits = model.prefill(torch.from_numpy(toks).to(cuda), torch.from_numpy(pos).to(cuda),
+                           torch.from_numpy(cu).to(cuda), max(lens), torch.from_numpy(slots).to(cuda), kv_e)
+    eager = layers.greedy_argmax(logits).cpu().numpy()
+    kv_g = KVCache(c.n_layers, nb, 16, c.n_kv_heads, c.head_dim, c.torch_dtype, cuda)
+    graph = model.capture_prefill(len(lens), 256, kv_g)
+    for t in kv_g.k_cache + kv_g.v_cache:
+        assert not t.any()
+    got = graph.run(toks, pos, lens, slots)
+    got2 = graph.run(toks, pos, lens, slots)
+    torch.cuda.synchronize()
+    assert np.array_equal(got, eager) and np.array_equal(got2, eager)
+    tol = 1e-4 if dtype == "float32" else 2e-2
+    used = torch.zeros(nb * 16, dtype=torch.bool, device=cuda)
+    used[torch.from_numpy(slots).to(cuda)] = True
+    for a, e in zip(kv_g.k_cache + kv_g.v_cache, kv_e.k_cache + kv_e.v_cache):
+        assert ((a.float() - e.float()).abs() <= tol * (1 + e.float().abs())).all()
+        assert not a.view(nb * 16, -1)[~used].any()
+    with pytest.raises(ValueError):
+        graph.run(toks, pos, lens[:2], slots)

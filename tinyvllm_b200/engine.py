@@ -39,6 +39,8 @@ from .model import KVCache, Llama
 
 _SAMPLING_EPS = 1e-5
 _GRAPH_BATCHES = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256, 384, 512)
+# prefill graphs hold a whole number of these tokens (the live prompts plus at least one padding token)
+_PREFILL_TOKEN_QUANTUM = 128
 
 
 @dataclass
@@ -209,6 +211,11 @@ class LLMEngine:
         # decode graphs, one per padded batch size (the reference keeps one TinyJit per batch size)
         self.use_cuda_graphs = use_cuda_graphs
         self._graphs = {}
+        # prefill graphs, one per (prompt count, padded token count); they replay one at
+        # a time on one stream, so they share one memory pool
+        self._prefill_graphs = {}
+        self._prefill_pool = None
+        self._prefill_stream = None
         self._graph_width = self.table_width or -(-2 * cfg.max_seq_len // block_size)
 
     # ------------------------------------------------------------------ API
@@ -325,11 +332,22 @@ class LLMEngine:
         pos = np.concatenate([np.arange(L, dtype=np.int32) for L in lens])
         cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
         dev = self.device
-        logits = self.model.prefill(torch.from_numpy(toks).to(dev), torch.from_numpy(pos).to(dev),
-                                    torch.from_numpy(cu).to(dev), max(lens), torch.from_numpy(slots).to(dev),
-                                    self.kv_cache)
-        sampled = self._sample(logits, seqs)
-        check_workspace(dev, "prefill", "prefill step")     # a kernel wait that timed out raises here
+        if self.use_cuda_graphs:
+            n, t_pad = len(seqs), -(-(int(cu[-1]) + 1) // _PREFILL_TOKEN_QUANTUM) * _PREFILL_TOKEN_QUANTUM
+            graph = self._prefill_graphs.get((n, t_pad))
+            if graph is None:
+                if self._prefill_pool is None:
+                    self._prefill_pool = torch.cuda.graph_pool_handle()
+                    self._prefill_stream = torch.cuda.Stream(dev)
+                graph = self.model.capture_prefill(n, t_pad, self.kv_cache, self._prefill_pool, self._prefill_stream)
+                self._prefill_graphs[(n, t_pad)] = graph
+            sampled = graph.run(toks, pos, lens, slots).tolist()   # raises if a kernel wait timed out
+        else:
+            logits = self.model.prefill(torch.from_numpy(toks).to(dev), torch.from_numpy(pos).to(dev),
+                                        torch.from_numpy(cu).to(dev), max(lens), torch.from_numpy(slots).to(dev),
+                                        self.kv_cache)
+            sampled = self._sample(logits, seqs)
+            check_workspace(dev, "prefill", "prefill step")     # a kernel wait that timed out raises here
         for s, L in zip(seqs, lens):
             bm.advance_position(s.seq_id, L)
         self.stats["prefill_tokens"] += int(sum(lens))

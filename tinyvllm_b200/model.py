@@ -190,12 +190,13 @@ class Llama:
 
     # ---------------------------------------------------------------- prefill
     def prefill(self, tokens: torch.Tensor, positions: torch.Tensor, cu_seqlens: torch.Tensor, max_seqlen: int,
-                slot_mapping: torch.Tensor, kv_cache: KVCache) -> torch.Tensor:
+                slot_mapping: torch.Tensor, kv_cache: KVCache, n_out: Optional[int] = None) -> torch.Tensor:
         """Ragged prefill of several prompts packed along tokens.
 
         tokens/positions int32 [T]; cu_seqlens int32 [n+1]; slot_mapping int64 [T].
         Writes every layer's post-RoPE K and raw V into ``kv_cache`` at the slots
-        (fused into the attention kernel) and returns the last-position logits [n, vocab].
+        (fused into the attention kernel) and returns the last-position logits
+        [n, vocab] (of the first ``n_out`` prompts only, when given).
         """
         c = self.config
         T = tokens.shape[0]
@@ -207,8 +208,14 @@ class Llama:
                                                   k_cache=kv_cache.k_cache[i], v_cache=kv_cache.v_cache[i])
             nxt = self.layers[i + 1].attention_norm if i + 1 < c.n_layers else self.norm
             x = self._layer_ffn(L, h, attn, nxt, T)
-        last = (cu_seqlens[1:] - 1).long()
-        return torch.matmul(x[last], self.output)
+        last = (cu_seqlens[1:] if n_out is None else cu_seqlens[1:n_out + 1]) - 1
+        return torch.matmul(x[last.long()], self.output)
+
+    def capture_prefill(self, n_prompts: int, padded_tokens: int, kv_cache: "KVCache",
+                        pool=None, stream: Optional[torch.cuda.Stream] = None) -> "PrefillGraph":
+        """A CUDA graph of one ragged prefill of ``n_prompts`` prompts totalling fewer
+        than ``padded_tokens`` tokens, plus the greedy pick of each prompt's first token."""
+        return PrefillGraph(self, n_prompts, padded_tokens, kv_cache, pool, stream)
 
     def capture_decode(self, batch: int, table_width: int, kv_cache: "KVCache",
                        kv_order: str = "reference") -> "DecodeGraph":
@@ -323,3 +330,97 @@ class DecodeGraph:
             raise _lib.TvkError("decode step: a bounded wait inside an attention kernel timed out; "
                                 "the step's tokens are not valid")
         return self.h_out.numpy()[:n].copy()
+
+
+class PrefillGraph:
+    """``Llama.prefill`` of ``n`` prompts followed by the greedy argmax, captured as a
+    CUDA graph over static buffers of ``T`` tokens.  The prompts fill the first
+    tokens; the rest of the buffer is one more (padding) prompt with token 0,
+    position 0 and slot -1, whose K/V is never stored and whose rows are
+    dropped, so every row the graph computes is finite and the real prompts see
+    the same kernels as an eager call (the projections run as GEMMs over ``T``
+    rows instead of the live count).  ``run`` copies a step's inputs from pinned
+    host memory into the buffers in one copy, replays the graph and returns the
+    sampled tokens; like ``DecodeGraph`` it raises ``TvkError`` if a bounded wait
+    inside an attention kernel of the step timed out.
+
+    An eager prefill step issues about ten launches per layer from Python, so
+    its length follows the host's speed; the graph issues one.
+    """
+
+    def __init__(self, model: Llama, n: int, T: int, kv_cache: KVCache, pool=None,
+                 stream: Optional[torch.cuda.Stream] = None):
+        if n < 1 or T < n + 1:
+            raise ValueError("a prefill graph needs n >= 1 prompts and T > n tokens")
+        dev = model.device
+        self.model, self.n, self.T, self.kv_cache = model, n, T, kv_cache
+        # one packed int32 staging buffer: tokens [T], positions [T], cu_seqlens [n + 2]
+        # (padded to an even count), then the slots as int64 [T]
+        self._off_cu = 2 * T
+        self._off_slots = 2 * T + ((n + 2 + 1) // 2) * 2
+        words = self._off_slots + 2 * T
+        self.h_in = torch.zeros(words, dtype=torch.int32).pin_memory()
+        self.d_in = torch.zeros(words, dtype=torch.int32, device=dev)
+        self.tok = self.d_in[:T]
+        self.pos = self.d_in[T:2 * T]
+        self.cu = self.d_in[self._off_cu:self._off_cu + n + 2]
+        self.slots = self.d_in[self._off_slots:].view(torch.int64)
+        self.out = torch.zeros(n + 1, dtype=torch.int32, device=dev)   # tokens, then the status word
+        self.h_out = torch.zeros(n + 1, dtype=torch.int32).pin_memory()
+        self._stage(np.zeros(0, np.int32), np.zeros(0, np.int32), None, np.zeros(0, np.int64))
+        self.d_in.copy_(self.h_in)
+        self.stream = stream or torch.cuda.Stream(dev)
+        self.stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(self.stream):
+            for _ in range(2):   # warm-up: workspaces, kernel attributes, cuBLAS handles
+                self._forward()
+        self.stream.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, pool=pool, stream=self.stream):
+            self._forward()
+        self.stream.synchronize()
+
+    def _forward(self):
+        m = self.model
+        logits = m.prefill(self.tok, self.pos, self.cu, self.T, self.slots, self.kv_cache, n_out=self.n)
+        layers.greedy_argmax(logits, out=self.out[:self.n])
+        # the attention calls used this stream's prefill workspace; the view keeps it
+        # alive for as long as the graph exists
+        self._status = status_word(m.device, "prefill")
+        self.out[self.n:].copy_(self._status)
+
+    def _stage(self, tokens, positions, lens, slots):
+        """Host staging: the prompts of ``lens`` (tokens, positions and slots
+        concatenated), then the padding prompt up to T tokens.  ``lens=None`` stages
+        the capture-time contents: n one-token prompts of token 0 that store nothing."""
+        h = self.h_in.numpy()
+        T, n = self.T, self.n
+        t_real = 0 if lens is None else int(sum(lens))
+        h[:t_real], h[t_real:T] = tokens, 0
+        h[T:T + t_real], h[T + t_real:2 * T] = positions, 0
+        cu = h[self._off_cu:self._off_cu + n + 2]
+        cu[0] = 0
+        cu[1:n + 1] = np.arange(1, n + 1) if lens is None else np.cumsum(lens)
+        cu[n + 1] = T
+        hs = h[self._off_slots:].view(np.int64)
+        hs[:t_real], hs[t_real:] = slots, -1
+
+    def run(self, tokens: np.ndarray, positions: np.ndarray, lens: List[int], slots: np.ndarray) -> np.ndarray:
+        if len(lens) != self.n or int(sum(lens)) >= self.T or min(lens) < 1:
+            raise ValueError("prompts do not fit the captured prefill graph")
+        self._stage(tokens, positions, lens, slots)
+        cur = torch.cuda.current_stream(self.model.device)
+        self.stream.wait_stream(cur)
+        with torch.cuda.stream(self.stream):
+            self.d_in.copy_(self.h_in, non_blocking=True)
+            self.graph.replay()
+            self.h_out.copy_(self.out, non_blocking=True)
+        self.stream.synchronize()
+        cur.wait_stream(self.stream)
+        if int(self.h_out[self.n]) != 0:
+            with torch.cuda.stream(self.stream):
+                self._status.zero_()
+            self.stream.synchronize()
+            raise _lib.TvkError("prefill step: a bounded wait inside an attention kernel timed out; "
+                                "the step's tokens are not valid")
+        return self.h_out.numpy()[:self.n].copy()
