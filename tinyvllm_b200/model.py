@@ -332,6 +332,34 @@ class DecodeGraph:
         return self.h_out.numpy()[:n].copy()
 
 
+def prefill_staging_layout(n: int, T: int):
+    """Word offsets of a prefill graph's packed int32 input buffer: tokens [T] at 0,
+    positions [T] at T, cu_seqlens [n + 2] at the first returned offset (padded to
+    an even count), the slots as int64 [T] at the second; the third value is the
+    buffer's length in int32 words."""
+    off_cu = 2 * T
+    off_slots = off_cu + ((n + 2 + 1) // 2) * 2
+    return off_cu, off_slots, off_slots + 2 * T
+
+
+def stage_prefill_inputs(h: np.ndarray, n: int, T: int, tokens, positions, lens, slots) -> None:
+    """Fill the packed buffer ``h`` (int32, ``prefill_staging_layout(n, T)``): the
+    prompts of ``lens`` (tokens, positions and slots concatenated) at the front,
+    then one padding prompt of token 0, position 0 and slot -1 up to T tokens, so
+    cu_seqlens = [0, prefix sums of lens..., T].  ``lens=None`` stages the
+    capture-time contents: n one-token prompts of token 0 that store nothing."""
+    off_cu, off_slots, _ = prefill_staging_layout(n, T)
+    t_real = 0 if lens is None else int(sum(lens))
+    h[:t_real], h[t_real:T] = tokens, 0
+    h[T:T + t_real], h[T + t_real:2 * T] = positions, 0
+    cu = h[off_cu:off_cu + n + 2]
+    cu[0] = 0
+    cu[1:n + 1] = np.arange(1, n + 1) if lens is None else np.cumsum(lens)
+    cu[n + 1] = T
+    hs = h[off_slots:off_slots + 2 * T].view(np.int64)
+    hs[:t_real], hs[t_real:] = slots, -1
+
+
 class PrefillGraph:
     """``Llama.prefill`` of ``n`` prompts followed by the greedy argmax, captured as a
     CUDA graph over static buffers of ``T`` tokens.  The prompts fill the first
@@ -354,11 +382,7 @@ class PrefillGraph:
             raise ValueError("a prefill graph needs n >= 1 prompts and T > n tokens")
         dev = model.device
         self.model, self.n, self.T, self.kv_cache = model, n, T, kv_cache
-        # one packed int32 staging buffer: tokens [T], positions [T], cu_seqlens [n + 2]
-        # (padded to an even count), then the slots as int64 [T]
-        self._off_cu = 2 * T
-        self._off_slots = 2 * T + ((n + 2 + 1) // 2) * 2
-        words = self._off_slots + 2 * T
+        self._off_cu, self._off_slots, words = prefill_staging_layout(n, T)
         self.h_in = torch.zeros(words, dtype=torch.int32).pin_memory()
         self.d_in = torch.zeros(words, dtype=torch.int32, device=dev)
         self.tok = self.d_in[:T]
@@ -390,20 +414,7 @@ class PrefillGraph:
         self.out[self.n:].copy_(self._status)
 
     def _stage(self, tokens, positions, lens, slots):
-        """Host staging: the prompts of ``lens`` (tokens, positions and slots
-        concatenated), then the padding prompt up to T tokens.  ``lens=None`` stages
-        the capture-time contents: n one-token prompts of token 0 that store nothing."""
-        h = self.h_in.numpy()
-        T, n = self.T, self.n
-        t_real = 0 if lens is None else int(sum(lens))
-        h[:t_real], h[t_real:T] = tokens, 0
-        h[T:T + t_real], h[T + t_real:2 * T] = positions, 0
-        cu = h[self._off_cu:self._off_cu + n + 2]
-        cu[0] = 0
-        cu[1:n + 1] = np.arange(1, n + 1) if lens is None else np.cumsum(lens)
-        cu[n + 1] = T
-        hs = h[self._off_slots:].view(np.int64)
-        hs[:t_real], hs[t_real:] = slots, -1
+        stage_prefill_inputs(self.h_in.numpy(), self.n, self.T, tokens, positions, lens, slots)
 
     def run(self, tokens: np.ndarray, positions: np.ndarray, lens: List[int], slots: np.ndarray) -> np.ndarray:
         if len(lens) != self.n or int(sum(lens)) >= self.T or min(lens) < 1:
