@@ -277,3 +277,16 @@ def test_prefill_graph_matches_eager_prefill(cuda, dtype):
         assert not a.view(nb * 16, -1)[~used].any()
     with pytest.raises(ValueError):
         graph.run(toks, pos, lens[:2], slots)
+
+
+def test_prefill_graph_cap_runs_further_shapes_eagerly(cuda, monkeypatch):
+    """Past its cap of prefill graphs an engine runs prefill steps of new shapes
+    eagerly; the streams stay those of an engine without the cap."""
+    from tinyvllm_b200 import engine as E
+    model = _tiny("float32", 128, 4, 2, seed=3)
+    prompts, max_toks = _requests(17, 6, 97, 5, 60, 3, 6)
+    ref, _ = _run_product(model, prompts, max_toks, max_batch_size=4, num_blocks=64, use_cuda_graphs=True)
+    monkeypatch.setattr(E, "_MAX_PREFILL_GRAPHS", 1)
+    got, eng = _run_product(model, prompts, max_toks, max_batch_size=4, num_blocks=64, use_cuda_graphs=True)
+    assert len(eng._prefill_graphs) == 1
+    assert got == ref

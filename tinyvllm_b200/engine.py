@@ -41,6 +41,8 @@ _SAMPLING_EPS = 1e-5
 _GRAPH_BATCHES = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256, 384, 512)
 # prefill graphs hold a whole number of these tokens (the live prompts plus at least one padding token)
 _PREFILL_TOKEN_QUANTUM = 128
+# prefill graphs an engine keeps; a step of another (prompt count, token count) shape runs eagerly
+_MAX_PREFILL_GRAPHS = 64
 
 
 @dataclass
@@ -332,9 +334,9 @@ class LLMEngine:
         pos = np.concatenate([np.arange(L, dtype=np.int32) for L in lens])
         cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
         dev = self.device
-        if self.use_cuda_graphs:
-            n, t_pad = len(seqs), -(-(int(cu[-1]) + 1) // _PREFILL_TOKEN_QUANTUM) * _PREFILL_TOKEN_QUANTUM
-            graph = self._prefill_graphs.get((n, t_pad))
+        n, t_pad = len(seqs), -(-(int(cu[-1]) + 1) // _PREFILL_TOKEN_QUANTUM) * _PREFILL_TOKEN_QUANTUM
+        graph = self._prefill_graphs.get((n, t_pad)) if self.use_cuda_graphs else None
+        if self.use_cuda_graphs and (graph is not None or len(self._prefill_graphs) < _MAX_PREFILL_GRAPHS):
             if graph is None:
                 if self._prefill_pool is None:
                     self._prefill_pool = torch.cuda.graph_pool_handle()
