@@ -14,7 +14,11 @@ iterations (engine.py:114-196), blocks freed when a sequence finishes
   pass (engine.py:235-255) and writes all sequences' new K/V with one launch
   per layer (the reference issues batch x layers writes, llama.py:381-386);
 * sampling is greedy only (temperature < 1e-5): an on-device argmax; the
-  reference's random sampling paths (sampling.py) are not part of this build.
+  reference's random sampling paths (sampling.py) are not part of this build;
+* with ``use_cuda_graphs`` a decode step replays a CUDA graph per padded batch
+  size and a prefill step one per (prompt count, token count rounded up to
+  128), the latter over a token buffer whose tail is a padding prompt that
+  stores nothing; up to 64 prefill graphs are kept, further shapes run eagerly.
 
 ``kv_order="reference"`` (default) reproduces the reference decode exactly:
 tables padded / truncated to 64 blocks (engine.py:81, llama.py:368-374),
